@@ -1,0 +1,376 @@
+"""Benchmark of the attention hot path (prints ONE JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (N > 1)
+
+Workload (Qwen3-32B layer): fused Q/K RMSNorm +
+RoPE + KV-cache write followed by causal GQA prefill attention, S = 4096,
+64 query / 8 KV heads, head_dim 128, f16, seeded N(0,1) inputs.  One step =
+both kernels over one sequence.  value = attention FLOPs (4*D*Hq*S(S+1)/2)
+per second of step time, whole job.  Multi-GPU: each rank runs its own
+sequence (weak scaling; attention shards by sequence / KV head with no
+collective).  Side measurements on rank 0 at N = 1: config 3's split-K
+decode grid (HBM GB/s per cell) and config 1.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Attn decode HBM GB/s + prefill TFLOP/s (Qwen3-32B GQA)"
+D = 128
+HQ, HKV, S = 64, 8, 4096
+EPS, THETA = 1e-6, 1.0e6
+L2_FLUSH_BYTES = 256 << 20
+
+
+def prefill_flops(S_, hq=HQ, P=0):
+    # causal, unmasked entries only: QK^T and PV, 2 flops per MAC each
+    return 4.0 * D * hq * sum_visible(S_, P)
+
+
+def sum_visible(S_, P=0):
+    return S_ * P + S_ * (S_ + 1) / 2.0
+
+
+def fused_bytes(S_, hq=HQ, hkv=HKV):
+    return 2.0 * S_ * (hq + 2 * hkv) * D * 2
+
+
+def peaks():
+    p = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            m = json.load(f)
+        p.update({k: m[k] for k in ("hbm_gbs", "bf16_tflops", "bf16_tflops_sustained") if k in m})
+        p["src"] = "measured"
+    return p
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.index)], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, x in enumerate(r) if x.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def make_inputs(seed_base):
+    from grout_b200 import synth
+    q = synth.normal(seed_base + 1, S * HQ * D).reshape(S, HQ, D)
+    k = synth.normal(seed_base + 2, S * HKV * D).reshape(S, HKV, D)
+    v = synth.normal(seed_base + 3, S * HKV * D).reshape(S, HKV, D)
+    qw = synth.norm_weight(seed_base + 4, D)
+    kw = synth.norm_weight(seed_base + 5, D)
+    return q, k, v, qw, kw
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_baseline(rows_step=64):
+    """The oracle (a C++ restatement of the reference's f32 CPU path) on a
+    bounded sample of the same workload: the fused norm/RoPE/KV write over
+    all 4096 tokens, and causal attention for every rows_step-th query row of
+    all 64 heads.  TFLOP/s = attention FLOPs of the sampled rows / time of
+    (sampled attention + fused write scaled to the same row fraction)."""
+    import oracle
+    q, k, v, qw, kw = make_inputs(0)
+    tab = oracle.rope_table(oracle.inv_freq(THETA, D), S)
+    kc = np.zeros((HKV, S, D), np.float16)
+    vc = np.zeros_like(kc)
+    t0 = time.perf_counter()
+    q_out = oracle.qk_norm_rope_kv_prefill(q, k, v, qw, kw, tab, kc, vc, 0, EPS)
+    t_fused = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    oracle.attn_prefill(q_out, kc, vc, np.array([0, S]), None, None, HQ, HKV, 0, D, S * D,
+                        1.0 / math.sqrt(D), rows_step=rows_step)
+    t_attn = time.perf_counter() - t0
+    rows = np.arange(0, S, rows_step)
+    flops = 4.0 * D * HQ * float(np.sum(rows + 1))
+    frac = len(rows) / S
+    t = t_attn + t_fused * frac
+    return {"value": flops / t / 1e12, "unit": "TFLOP/s", "cores": oracle.num_threads(),
+            "kind": "port",
+            "sample": f"oracle: attention for every {rows_step}th query row (64 of 4096) x 64 heads "
+                      f"+ fused norm/RoPE/KV write (full, time scaled by {frac:.4f}); "
+                      f"{t_attn:.2f}s + {t_fused:.2f}s"}
+
+
+# ------------------------------------------------------------ GPU arm
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import grout_b200 as g
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    g.init(local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    q, k, v, qw, kw = make_inputs(1000 * rank)
+    pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+    hq_, hk_, hv_ = pin(q), pin(k), pin(v)
+    dq, dk, dv = hq_.to(dev), hk_.to(dev), hv_.to(dev)
+    dqw, dkw = pin(qw).to(dev), pin(kw).to(dev)
+    table = g.rope_table(THETA, S, dev)
+    kc = torch.zeros(HKV, S, D, dtype=torch.float16, device=dev)
+    vc = torch.zeros_like(kc)
+    q_out = torch.empty_like(dq)
+    out = torch.empty_like(dq)
+    host_out = torch.empty(out.shape, dtype=torch.float16).pin_memory()
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        g.qk_norm_rope_kv_prefill(dq, dk, dv, dqw, dkw, table, q_out, kc, vc, 0, EPS)
+        g.attention_prefill(q_out, kc, vc, out, 0)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    g.check_device_error()
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        for i in range(args.steps):
+            flush.fill_(float(i))  # L2 flush between timed steps (outside the events)
+            ev[i][0].record(stream)
+            g.qk_norm_rope_kv_prefill(dq, dk, dv, dqw, dkw, table, q_out, kc, vc, 0, EPS)
+            ev[i][1].record(stream)
+            g.attention_prefill(q_out, kc, vc, out, 0)
+            ev[i][2].record(stream)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    step_ms = sum(e[0].elapsed_time(e[2]) for e in ev)
+    fused_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
+    attn_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
+    g.check_device_error()
+
+    # end to end through the public API with host buffers
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(2):
+        dq.copy_(hq_, non_blocking=True)
+        step()
+        host_out.copy_(out, non_blocking=True)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        dq.copy_(hq_, non_blocking=True)
+        dk.copy_(hk_, non_blocking=True)
+        dv.copy_(hv_, non_blocking=True)
+        g.qk_norm_rope_kv_prefill(dq, dk, dv, dqw, dkw, table, q_out, kc, vc, 0, EPS)
+        g.attention_prefill(q_out, kc, vc, out, 0)
+        host_out.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+
+    times = torch.tensor([step_ms, e2e_ms, attn_ms, fused_ms], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    step_ms, e2e_ms, attn_ms, fused_ms = times.tolist()
+    if rank != 0:
+        return None
+
+    pk = peaks()
+    flops = prefill_flops(S)
+    ms_per_step = step_ms / args.steps
+    value = world * flops * args.steps / (step_ms * 1e-3) / 1e12
+    achieved = flops / (attn_ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded N(0,1) f16 inputs; norm weights 1+N(0,0.02))",
+        "config": {"workload": "C2: fused Q/K RMSNorm+RoPE+KV write -> causal GQA prefill, "
+                               "Qwen3-32B layer, S=4096, Hq=64, Hkv=8, D=128, batch 1 per GPU",
+                   "seq_len": S, "num_q_heads": HQ, "num_kv_heads": HKV, "head_dim": D,
+                   "l2": "flushed between timed steps (256 MB write outside the events)",
+                   "parallelism": f"sequence-sharded x{world} (no collective)"},
+        "roofline": {"bound": "tensor", "kernel": "prefill_kernel (tcgen05)",
+                     "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(achieved / pk["bf16_tflops"], 4),
+                     "peak_src": pk["src"] + " bf16 burst (dense f16 == bf16 rate on B200)",
+                     "traffic": None, "kernel_ms": round(attn_ms, 4),
+                     "algorithmic_flops": flops},
+        "fused_norm_rope_kv": {"bound": "hbm", "ms": round(fused_ms, 4),
+                               "gbs": round(fused_bytes(S) / (fused_ms * 1e-3) / 1e9, 1),
+                               "frac": round(fused_bytes(S) / (fused_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+                               "algorithmic_bytes": fused_bytes(S)},
+        "e2e": {"value": round(world * flops * args.steps / (e2e_ms * 1e-3) / 1e12, 2),
+                "unit": "TFLOP/s", "h2d_bytes_per_step": int(hq_.numel() * 2 + hk_.numel() * 2 + hv_.numel() * 2),
+                "d2h_bytes_per_step": int(host_out.numel() * 2),
+                "ms_per_step": round(e2e_ms / args.steps, 4),
+                "path": "grout_b200.qk_norm_rope_kv_prefill + attention_prefill, pinned host buffers"},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_decode:
+        line["decode"] = decode_grid(args, dev, pk)
+    if world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline()
+    return line
+
+
+def decode_grid(args, dev, pk):
+    """Config 3: split-K decode over B x L cells (Qwen3-32B, 64/8 heads), and
+    config 1 (Qwen3-4B, 32/8 heads, L = 1024).  HBM bytes per cell:
+    B*(2*Hkv*L*D*2 + 2*Hq*D*2).  Each rep is timed alone with an L2 flush
+    before it."""
+    import torch
+    import grout_b200 as g
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    cells = []
+    shapes = [(1, 32, 8, 1024)] + [(B, 64, 8, L) for B in (1, 8, 32, 64)
+                                   for L in (2048, 8192, 16384, 32768)]
+    reps = max(3, min(args.steps, 10))
+    for B, hq, hkv, L in shapes:
+        kc = torch.randn(B, hkv, L, D, device=dev, dtype=torch.float16)
+        vc = torch.randn_like(kc)
+        q = torch.randn(B, hq, D, device=dev, dtype=torch.float16)
+        out = torch.empty_like(q)
+        pos = torch.full((B,), L - 1, dtype=torch.int32, device=dev)
+        nks = g.decode_splits(B, L, hq, hkv, L)
+        ws = torch.empty(max(16, g.decode_workspace_bytes(B, L, hq, hkv, L)), dtype=torch.uint8, device=dev)
+        for _ in range(3):
+            g.attention_decode(q, kc, vc, pos, out, L, workspace=ws)
+        ts = []
+        for _ in range(reps):
+            flush.fill_(1.0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.attention_decode(q, kc, vc, pos, out, L, workspace=ws)
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        us = statistics.median(ts) * 1e3
+        nbytes = B * (2 * hkv * L * D * 2 + 2 * hq * D * 2)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        cells.append({"B": B, "L": L, "hq": hq, "splits": nks, "us": round(us, 2),
+                      "gbs": round(gbs, 1), "frac": round(gbs / pk["hbm_gbs"], 4)})
+        del kc, vc
+        torch.cuda.empty_cache()
+    g.check_device_error()
+    big = [c for c in cells if c["B"] * c["L"] >= 8 * 8192]
+    return {"unit": "GB/s", "peak_gbs": pk["hbm_gbs"], "cells": cells,
+            "mean_frac_large_cells": round(statistics.mean(c["frac"] for c in big), 4)}
+
+
+# ------------------------------------------------------------ reference arm
+def run_reference(args):
+    """The reference's CPU path for the same workload (the oracle port; the
+    Rust reference cannot be built here), all host threads, K timed steps
+    each on the bounded sample."""
+    import oracle
+    for _ in range(args.warmup):
+        pass
+    vals = []
+    last = None
+    for _ in range(args.steps):
+        last = cpu_baseline(rows_step=256)
+        vals.append(last["value"])
+    v = statistics.median(vals)
+    return {"metric": METRIC, "value": round(v, 6), "unit": "TFLOP/s", "impl": "reference",
+            "n_gpus": 0, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) f16 inputs)",
+            "config": {"workload": "C2: fused Q/K RMSNorm+RoPE+KV write -> causal GQA prefill, "
+                                   "Qwen3-32B layer, S=4096, Hq=64, Hkv=8, D=128",
+                       "seq_len": S},
+            "cpu_baseline": {"value": round(v, 6), "unit": "TFLOP/s", "cores": oracle.num_threads(),
+                             "kind": "port", "sample": last["sample"]},
+            "e2e": {"value": round(v, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return
+
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    line = run_ours(args, rank, world, local_rank)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

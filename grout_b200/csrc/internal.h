@@ -1,0 +1,83 @@
+// Internal launch interface between the C ABI (abi.cu) and the kernels.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace grout {
+
+constexpr int kHeadDim = 128;
+
+struct NormRopeArgs {
+  const __half* q;     // prefill: q rows; decode: qkv rows
+  const __half* k;     // prefill only
+  const __half* v;     // prefill only
+  int64_t q_row_stride;   // prefill: q/q_out row stride; decode: qkv row length
+  int64_t kv_row_stride;  // prefill only
+  const __half* q_w;
+  const __half* k_w;
+  const float* table;
+  __half* q_out;
+  __half* k_cache;
+  __half* v_cache;
+  int64_t cache_batch_stride;  // decode only
+  int64_t cache_head_stride;
+  const uint32_t* d_position;  // decode only
+  int32_t pos0;                // prefill only
+  int32_t rows;                // prefill: seq_len; decode: batch
+  int32_t hq;
+  int32_t hkv;
+  int32_t max_seq;
+  float eps;
+  int32_t decode;
+  int* err;
+};
+
+cudaError_t launch_qk_norm_rope_kv(const NormRopeArgs& a, int num_sms, cudaStream_t s);
+
+struct DecodeArgs {
+  const __half* q;      // [B][hq][128]
+  __half* out;          // [B][hq][128]
+  float* part_o;        // [B][hq][nks][128] (nks > 1)
+  float* part_lse;      // [B][hq][nks]      (nks > 1)
+  const uint32_t* d_position;
+  int32_t batch;
+  int32_t hq;
+  int32_t hkv;
+  int32_t nks;
+  float scale_log2;
+  int* err;
+};
+
+// tm_k / tm_v: 4-D maps {128, max_seq, hkv, batch} over the caches, box
+// {64, 64, 1, 1}, 128B swizzle.
+cudaError_t launch_decode(const DecodeArgs& a, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                          cudaStream_t s);
+cudaError_t decode_set_attributes();
+
+struct PrefillArgs {
+  __half* out;
+  int64_t q_row_stride;
+  const int32_t* cu_q;       // device [B+1]
+  const int32_t* pos0;       // device [B] or null
+  const int32_t* kv_start;   // device [B] or null
+  int32_t batch;
+  int32_t max_q_len;
+  int32_t hq;
+  int32_t hkv;
+  int32_t kv_batched;        // K/V maps carry a batch coordinate
+  int32_t single_len;        // used when cu_q == null (batch 1)
+  int32_t single_pos0;       // used when pos0 == null
+  float scale_log2;
+  int* err;
+};
+
+// tm_q: 3-D {128, hq, q_rows}, box {64, 1, 128}; tm_k / tm_v: 4-D
+// {128, kv_rows, hkv, B} (or 3-D without the batch dim), box {64, 128, 1(,1)};
+// all 128B swizzle.
+cudaError_t launch_prefill(const PrefillArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                           const CUtensorMap& tm_v, cudaStream_t s);
+cudaError_t prefill_set_attributes();
+
+}  // namespace grout

@@ -1,0 +1,339 @@
+// Causal GQA prefill attention on the 5th-generation tensor cores.
+//
+// Replaces fmha_prefill_causal / fmha_prefill_gqa_lpt (reference
+// src/kernels.rs:2570-2725, 2943-3298) and flash_attn_causal_seq_f16
+// (2462-2557): O = softmax(scale * Q K^T + causal mask) V per query head,
+// f16 in, f32 accumulate, P rounded to f16 before the PV product, f16 out.
+//
+// One CTA = two 128-row query tiles of one head (256 query rows), streaming
+// 128-key K/V tiles.  Warp roles (320 threads):
+//   warps 0-3  softmax for query tile 0 (one thread per query row = TMEM lane)
+//   warps 4-7  softmax for query tile 1
+//   warp 8     TMA producer: Q tiles once, then K_j, V_j into a 4-slot ring
+//   warp 9     MMA issuer (one thread): tcgen05.mma, completion via
+//              tcgen05.commit on mbarriers
+// Tensor memory (512 columns, f32): S0 [0,128) S1 [128,256) O0 [256,384)
+// O1 [384,512).  P_t (f16 pairs) overwrites the first 64 columns of S_t and
+// feeds the PV MMA straight from TMEM (A operand in TMEM, V from shared
+// memory), so P never touches shared memory.
+// Per KV tile j the MMA warp issues PV0(j), QK0(j+1), PV1(j), QK1(j+1):
+// the next S of one query tile is computed while the other tile's softmax
+// runs.  Because tcgen05 operations of one thread complete in issue order,
+// "S_t(j+1) ready" also means "PV_t(j) done", which is what the softmax
+// warps need before they rescale O_t in place.
+// Scheduling: blockIdx.y walks query-tile pairs from the last (longest
+// causal row range) to the first, so the heaviest CTAs start first;
+// blockIdx.x is the query head, so the G heads that share a KV head run
+// side by side and reuse its K/V through L2.
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace grout {
+namespace {
+
+constexpr int kBM = 128;          // query rows per tile (= TMEM lanes)
+constexpr int kBN = 128;          // keys per KV tile
+constexpr int kSlots = 4;         // K/V ring slots
+constexpr int kTile = 128 * 128 * 2;  // bytes of one 128x128 f16 tile (two 64-col boxes)
+constexpr int kBox = kTile / 2;
+constexpr int kThreads = 320;
+constexpr int kOffQ = 0;                       // 2 query tiles
+constexpr int kOffKV = 2 * kTile;              // ring
+constexpr int kOffBar = kOffKV + kSlots * kTile;
+constexpr int kSmemBytes = kOffBar + 256 + 1024;
+
+// barrier indices
+constexpr int kBarQ = 0;
+constexpr int kBarFull = 1;                 // + slot
+constexpr int kBarEmpty = kBarFull + kSlots;  // + slot
+constexpr int kBarS = kBarEmpty + kSlots;   // + tile
+constexpr int kBarP = kBarS + 2;            // + tile
+constexpr int kBarO = kBarP + 2;
+constexpr int kNumBars = kBarO + 1;
+
+__device__ __forceinline__ int ring_slot(int i) { return i % kSlots; }
+__device__ __forceinline__ uint32_t ring_parity(int i) { return (uint32_t)((i / kSlots) & 1); }
+
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int h = blockIdx.x;
+  const int b = blockIdx.z;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  int q_start, S, P, ks;
+  if (a.cu_q) {
+    q_start = a.cu_q[b];
+    S = a.cu_q[b + 1] - q_start;
+  } else {
+    q_start = 0;
+    S = a.single_len;
+  }
+  P = a.pos0 ? a.pos0[b] : a.single_pos0;
+  ks = a.kv_start ? a.kv_start[b] : 0;
+  const int n_pairs = (a.max_q_len + 2 * kBM - 1) / (2 * kBM);
+  const int pair = n_pairs - 1 - (int)blockIdx.y;
+  const int q0 = pair * 2 * kBM;
+  if (q0 >= S) return;  // ragged batch: this sequence is shorter
+  const int rows_hi = min(q0 + 2 * kBM, S);
+  const int kv_len = P + S;
+  const int n_kv = (P + rows_hi + kBN - 1) / kBN;
+  const int kh = h / (a.hq / a.hkv);
+  const int kvb = a.kv_batched ? b : 0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kNumBars; ++i) {
+      uint32_t cnt = 1;
+      if (i == kBarP || i == kBarP + 1) cnt = kBM;
+      mbar_init(smem_u32(&bars[i]), cnt);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_holder), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t smem_base = smem_u32(smem);
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_q);
+      prefetch_tmap(&tm_k);
+      prefetch_tmap(&tm_v);
+      const uint32_t bq = smem_u32(&bars[kBarQ]);
+      mbar_arrive_expect_tx(bq, 2 * kTile);
+      for (int t = 0; t < 2; ++t) {
+        const uint32_t dst = smem_base + kOffQ + t * kTile;
+        const int row = q_start + q0 + t * kBM;
+        tma_load_3d(dst, &tm_q, bq, 0, h, row);
+        tma_load_3d(dst + kBox, &tm_q, bq, 64, h, row);
+      }
+      for (int i = 0; i < 2 * n_kv; ++i) {
+        const int slot = ring_slot(i);
+        if (i >= kSlots &&
+            !mbar_wait(smem_u32(&bars[kBarEmpty + slot]), ring_parity(i) ^ 1u, a.err, 10,
+                       abort_flag))
+          break;
+        const uint32_t full = smem_u32(&bars[kBarFull + slot]);
+        mbar_arrive_expect_tx(full, kTile);
+        const CUtensorMap* map = (i & 1) ? &tm_v : &tm_k;
+        const uint32_t dst = smem_base + kOffKV + slot * kTile;
+        const int row = ks + (i >> 1) * kBN;
+        if (a.kv_batched) {
+          tma_load_4d(dst, map, full, 0, row, kh, kvb);
+          tma_load_4d(dst + kBox, map, full, 64, row, kh, kvb);
+        } else {
+          tma_load_3d(dst, map, full, 0, row, kh);
+          tma_load_3d(dst + kBox, map, full, 64, row, kh);
+        }
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------- MMA issue
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = idesc_f16_f32(kBM, kBN, 0, 0);
+      constexpr uint32_t idesc_pv = idesc_f16_f32(kBM, 128, 0, 1);
+      const uint32_t tS[2] = {tmem + 0, tmem + 128};
+      const uint32_t tO[2] = {tmem + 256, tmem + 384};
+      auto qk = [&](int t, int slot) {
+        const uint32_t qa = smem_base + kOffQ + t * kTile;
+        const uint32_t kb = smem_base + kOffKV + slot * kTile;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
+          tc_mma_ss(tS[t], smem_desc_sw128(qa + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024),
+                    idesc_qk, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto pv = [&](int t, int slot, bool acc) {
+        const uint32_t vb = smem_base + kOffKV + slot * kTile;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          tc_mma_ts(tO[t], tS[t] + kk * 8, smem_desc_sw128(vb + kk * 2048, kBox, 1024), idesc_pv,
+                    (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(smem_u32(&bars[kBarQ]), 0, a.err, 20, abort_flag);
+      ok = ok && mbar_wait(smem_u32(&bars[kBarFull + ring_slot(0)]), ring_parity(0), a.err, 21,
+                           abort_flag);
+      if (ok) {
+        tc_fence_after();
+        qk(0, ring_slot(0));
+        tc_commit(smem_u32(&bars[kBarS + 0]));
+        qk(1, ring_slot(0));
+        tc_commit(smem_u32(&bars[kBarS + 1]));
+        tc_commit(smem_u32(&bars[kBarEmpty + ring_slot(0)]));
+        for (int j = 0; j < n_kv && ok; ++j) {
+          const int iv = 2 * j + 1, ik = 2 * j + 2;
+          const bool next = j + 1 < n_kv;
+          ok = mbar_wait(smem_u32(&bars[kBarFull + ring_slot(iv)]), ring_parity(iv), a.err, 22,
+                         abort_flag);
+          ok = ok && mbar_wait(smem_u32(&bars[kBarP + 0]), j & 1, a.err, 23, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          pv(0, ring_slot(iv), j > 0);
+          if (next) {
+            ok = mbar_wait(smem_u32(&bars[kBarFull + ring_slot(ik)]), ring_parity(ik), a.err, 24,
+                           abort_flag);
+            if (!ok) break;
+            tc_fence_after();
+            qk(0, ring_slot(ik));
+            tc_commit(smem_u32(&bars[kBarS + 0]));
+          }
+          ok = mbar_wait(smem_u32(&bars[kBarP + 1]), j & 1, a.err, 25, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          pv(1, ring_slot(iv), j > 0);
+          tc_commit(smem_u32(&bars[kBarEmpty + ring_slot(iv)]));
+          if (next) {
+            qk(1, ring_slot(ik));
+            tc_commit(smem_u32(&bars[kBarS + 1]));
+            tc_commit(smem_u32(&bars[kBarEmpty + ring_slot(ik)]));
+          }
+        }
+        tc_commit(smem_u32(&bars[kBarO]));
+      }
+    }
+  } else {
+    // --------------------------------------------------------------- softmax
+    const int t = warp >> 2;          // query tile
+    const int row = threadIdx.x & 127;  // TMEM lane == query row within the tile
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + t * 128 + lane_off;
+    const uint32_t tO = tmem + 256 + t * 128 + lane_off;
+    const int row_q = q0 + t * kBM + row;
+    const int key_lim = min(P + row_q, kv_len - 1);  // last visible key
+    const float sl2 = a.scale_log2;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      ok = mbar_wait(smem_u32(&bars[kBarS + t]), j & 1, a.err, 30 + t, abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      float s[128];
+      {
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(tS + c * 32, r);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+        }
+      }
+      const int lim = key_lim - j * kBN;
+      if (lim < kBN - 1) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (c > lim) s[c] = -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int c = 1; c < 128; ++c) mx = fmaxf(mx, s[c]);
+      const float m_new = fmaxf(m, mx * sl2);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = ex2(m - m_use);
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = ex2(fmaf(s[c * 32 + 2 * i], sl2, -m_use));
+          const float p1 = ex2(fmaf(s[c * 32 + 2 * i + 1], sl2, -m_use));
+          rs += p0 + p1;
+          pk[i] = pack_half2(p0, p1);
+        }
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, "
+            "%10, %11, %12, %13, %14, %15, %16};" ::"r"(tS + c * 16),
+            "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3]), "r"(pk[4]), "r"(pk[5]), "r"(pk[6]),
+            "r"(pk[7]), "r"(pk[8]), "r"(pk[9]), "r"(pk[10]), "r"(pk[11]), "r"(pk[12]),
+            "r"(pk[13]), "r"(pk[14]), "r"(pk[15])
+            : "memory");
+      }
+      l = l * alpha + rs;
+      // Rescale O_t when the running max moved (PV_t(j-1) has completed:
+      // it was issued before the QK that produced this S).
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tO + c * 32, r);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st32(tO + c * 32, r);
+        }
+      }
+      tc_wait_st();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&bars[kBarP + t]));
+      m = m_new;
+    }
+    if (ok) ok = mbar_wait(smem_u32(&bars[kBarO]), 0, a.err, 40, abort_flag);
+    if (ok) {
+      tc_fence_after();
+      const float inv_l = 1.0f / fmaxf(l, 1.0e-8f);
+      const bool valid = row_q < S;
+      __half* orow = a.out + (int64_t)(q_start + row_q) * a.q_row_stride + (int64_t)h * 128;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tO + c * 32, r);
+        tc_wait_ld();
+        if (valid) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 u;
+            u.x = pack_half2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
+            u.y = pack_half2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
+            u.z = pack_half2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
+            u.w = pack_half2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
+            dst[v] = u;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+cudaError_t prefill_set_attributes() {
+  return cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              kSmemBytes);
+}
+
+cudaError_t launch_prefill(const PrefillArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                           const CUtensorMap& tm_v, cudaStream_t s) {
+  const int n_pairs = (a.max_q_len + 2 * kBM - 1) / (2 * kBM);
+  if (n_pairs == 0 || a.batch == 0) return cudaSuccess;
+  dim3 grid(a.hq, n_pairs, a.batch);
+  prefill_kernel<<<grid, kThreads, kSmemBytes, s>>>(tm_q, tm_k, tm_v, a);
+  return cudaGetLastError();
+}
+
+}  // namespace grout

@@ -1,0 +1,127 @@
+"""CPU checks of the C ABI: the library builds, loads, exports every symbol
+include/grout_attn.h declares, and its host-only logic (argument validation,
+inv_freq, split selection) behaves; no kernel is launched."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+import oracle
+from grout_b200 import attn, build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "grout_attn.h")
+
+
+def header_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(grout_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def L():
+    build.build()
+    return attn.lib()
+
+
+def test_every_declared_symbol_is_exported_and_bound(L):
+    names = header_functions()
+    assert len(names) >= 14
+    for n in names:
+        assert hasattr(L, n), n
+    # the Python mirror binds exactly the declared set
+    assert sorted(attn.SIGNATURES) == names
+
+
+def test_version_and_empty_error(L):
+    assert b"sm_100a" in L.grout_attn_version()
+    assert L.grout_attn_last_error() is not None
+
+
+def test_inv_freq_matches_oracle(L):
+    for theta in (1.0e4, 1.0e6, 5.0e5):
+        a = attn.inv_freq(theta)
+        b = oracle.inv_freq(theta, 128)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_rope_table_bytes(L):
+    assert L.grout_rope_table_bytes(4096, 128) == 4096 * 128 * 4
+    assert L.grout_rope_table_bytes(0, 128) == 0
+
+
+def _dims(hq=64, hkv=8, hd=128, ms=4096):
+    return attn.AttnDims(hq, hkv, hd, ms, 1e-6, 0.0, 0)
+
+
+def _err(L):
+    return L.grout_attn_last_error().decode()
+
+
+def test_validation_before_launch(L):
+    """Shape/range errors are reported as INVALID_ARG / UNSUPPORTED without
+    touching a device (this container has none)."""
+    p = ctypes.c_void_p(0x10000)  # aligned, never dereferenced
+    d = _dims(hd=64)
+    st = L.grout_attn_prefill(p, p, p, p, 4096 * 128, 0, 16, ctypes.byref(d), None)
+    assert st == 2 and "head_dim" in _err(L)
+    d = _dims()
+    st = L.grout_attn_prefill(p, p, p, p, 4096 * 128, 4090, 16, ctypes.byref(d), None)
+    assert st == 1 and "exceeds max_seq" in _err(L)
+    st = L.grout_qk_norm_rope_kv_prefill(p, p, p, 64 * 128, 8 * 128, p, p, p, p, p, p,
+                                         4096 * 128, 4095, 2, ctypes.byref(d), None)
+    assert st == 1 and "exceeds max_seq" in _err(L)
+    st = L.grout_qk_norm_rope_kv_prefill(p, None, p, 64 * 128, 8 * 128, p, p, p, p, p, p,
+                                         4096 * 128, 0, 2, ctypes.byref(d), None)
+    assert st == 1 and "null" in _err(L)
+    bad = ctypes.c_void_p(0x10002)
+    st = L.grout_qk_norm_rope_kv_prefill(p, bad, p, 64 * 128, 8 * 128, p, p, p, p, p, p,
+                                         4096 * 128, 0, 2, ctypes.byref(d), None)
+    assert st == 1 and "aligned" in _err(L)
+    d = _dims(hq=64, hkv=4)  # group 16 > 8
+    st = L.grout_attn_decode(p, p, p, 0, 4096 * 128, p, p, 1, 100, ctypes.byref(d), None, 0, None)
+    assert st == 2 and "group" in _err(L)
+    d = _dims()
+    st = L.grout_attn_decode_ex(p, p, p, 0, 4096 * 128, p, p, 1, 5000, 4, ctypes.byref(d), None, 0, None)
+    assert st == 1 and "max_kv_len" in _err(L)
+    st = L.grout_attn_decode_ex(p, p, p, 0, 4096 * 128, p, p, 1, 4096, 4, ctypes.byref(d), None, 0, None)
+    assert st == 1 and "workspace" in _err(L)
+    d = _dims(hq=63, hkv=8)
+    st = L.grout_attn_prefill(p, p, p, p, 4096 * 128, 0, 16, ctypes.byref(d), None)
+    assert st == 1 and "multiple" in _err(L)
+
+
+def test_init_without_gpu_fails_cleanly(L):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    st = L.grout_attn_init(0)
+    assert st == 3 and _err(L)
+
+
+def test_decode_split_heuristic(L):
+    """Split count: >= 1 split per 2048 keys, >= 128 keys per split, enough
+    CTAs to fill 148 SMs when the sequence allows it."""
+    for B in (1, 8, 32, 64):
+        for Lk in (2048, 8192, 16384, 32768):
+            n = attn.decode_splits(B, Lk, 64, 8, 32768)
+            tiles = Lk // 64
+            assert 1 <= n <= max(1, tiles // 2)
+            assert Lk / n <= 2048 + 64
+            if B * 8 * tiles // 2 >= 2 * 148:
+                assert B * 8 * n >= 148
+    assert attn.decode_splits(1, 64, 64, 8, 32768) == 1
+    assert attn.decode_workspace_bytes(1, 64, 64, 8, 32768) == 0
+    n = attn.decode_splits(8, 8192, 64, 8, 32768)
+    assert attn.decode_workspace_bytes(8, 8192, 64, 8, 32768) == 8 * 64 * n * 129 * 4
+
+
+def test_python_mirror_rejects_cpu_tensors():
+    import torch
+    q = torch.zeros(4, 8, 128, dtype=torch.float16)
+    with pytest.raises(attn.GroutError):
+        attn.attention_prefill(q, torch.zeros(2, 16, 128, dtype=torch.float16),
+                               torch.zeros(2, 16, 128, dtype=torch.float16), q.clone())
