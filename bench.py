@@ -31,6 +31,9 @@ D = 128
 HQ, HKV, S = 64, 8, 4096
 EPS, THETA = 1e-6, 1.0e6
 L2_FLUSH_BYTES = 256 << 20
+# DRAM bytes (read + write) of one prefill_kernel launch on this workload,
+# from the ncu capture summarised in profiles/prefill_kernel_qwen3_32b_s4096.md
+PREFILL_TRAFFIC_BYTES = 83_973_632 + 25_476_352
 
 
 def prefill_flops(S_, hq=HQ, P=0):
@@ -40,6 +43,30 @@ def prefill_flops(S_, hq=HQ, P=0):
 
 def sum_visible(S_, P=0):
     return S_ * P + S_ * (S_ + 1) / 2.0
+
+
+def shard_kv_heads(hkv, world, rank):
+    """KV heads [lo, hi) owned by `rank` when a layer is sharded by KV head
+    (each rank also owns query heads [lo*G, hi*G)); no exchange is needed."""
+    if hkv % world:
+        raise ValueError(f"{hkv} KV heads do not split over {world} ranks")
+    per = hkv // world
+    return rank * per, (rank + 1) * per
+
+
+def reduce_max(values, dist=None, device=None):
+    """Max over ranks of a list of per-rank timings (ms)."""
+    if dist is None:
+        return list(values)
+    import torch
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def job_tflops(flops_per_rank_step, steps, world, max_ms):
+    """Whole-job throughput: every rank's work over the slowest rank's time."""
+    return world * flops_per_rank_step * steps / (max_ms * 1e-3) / 1e12
 
 
 def fused_bytes(S_, hq=HQ, hkv=HKV):
@@ -118,7 +145,7 @@ def make_inputs(seed_base):
 
 
 # ------------------------------------------------------------ CPU baseline
-def cpu_baseline(rows_step=64):
+def cpu_baseline(rows_step=2):
     """The oracle (a C++ restatement of the reference's f32 CPU path) on a
     bounded sample of the same workload: the fused norm/RoPE/KV write over
     all 4096 tokens, and causal attention for every rows_step-th query row of
@@ -142,12 +169,28 @@ def cpu_baseline(rows_step=64):
     t = t_attn + t_fused * frac
     return {"value": flops / t / 1e12, "unit": "TFLOP/s", "cores": oracle.num_threads(),
             "kind": "port",
-            "sample": f"oracle: attention for every {rows_step}th query row (64 of 4096) x 64 heads "
+            "sample": f"oracle: attention for every {rows_step}th query row ({len(rows)} of 4096) x 64 heads "
                       f"+ fused norm/RoPE/KV write (full, time scaled by {frac:.4f}); "
                       f"{t_attn:.2f}s + {t_fused:.2f}s"}
 
 
 # ------------------------------------------------------------ GPU arm
+def capture(fn):
+    """Warm `fn` up on a side stream, capture it into a CUDA graph."""
+    import torch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    torch.cuda.synchronize()
+    return graph
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import grout_b200 as g
@@ -181,6 +224,11 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     g.check_device_error()
 
+    # Each kernel is captured once into a CUDA graph (as the engine records
+    # its decode step) so the timed region holds device work only, not the
+    # Python/ctypes launch path.
+    g_fused = capture(lambda: g.qk_norm_rope_kv_prefill(dq, dk, dv, dqw, dkw, table, q_out, kc, vc, 0, EPS))
+    g_attn = capture(lambda: g.attention_prefill(q_out, kc, vc, out, 0))
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     if dist:
         dist.barrier()
@@ -189,9 +237,9 @@ def run_ours(args, rank, world, local_rank):
         for i in range(args.steps):
             flush.fill_(float(i))  # L2 flush between timed steps (outside the events)
             ev[i][0].record(stream)
-            g.qk_norm_rope_kv_prefill(dq, dk, dv, dqw, dkw, table, q_out, kc, vc, 0, EPS)
+            g_fused.replay()
             ev[i][1].record(stream)
-            g.attention_prefill(q_out, kc, vc, out, 0)
+            g_attn.replay()
             ev[i][2].record(stream)
         torch.cuda.synchronize()
     if dist:
@@ -222,17 +270,14 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
 
-    times = torch.tensor([step_ms, e2e_ms, attn_ms, fused_ms], dtype=torch.float64, device=dev)
-    if dist:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    step_ms, e2e_ms, attn_ms, fused_ms = times.tolist()
+    step_ms, e2e_ms, attn_ms, fused_ms = reduce_max([step_ms, e2e_ms, attn_ms, fused_ms], dist, dev)
     if rank != 0:
         return None
 
     pk = peaks()
     flops = prefill_flops(S)
     ms_per_step = step_ms / args.steps
-    value = world * flops * args.steps / (step_ms * 1e-3) / 1e12
+    value = job_tflops(flops, args.steps, world, step_ms)
     achieved = flops / (attn_ms * 1e-3) / 1e12
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
@@ -248,13 +293,13 @@ def run_ours(args, rank, world, local_rank):
                      "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": round(achieved / pk["bf16_tflops"], 4),
                      "peak_src": pk["src"] + " bf16 burst (dense f16 == bf16 rate on B200)",
-                     "traffic": None, "kernel_ms": round(attn_ms, 4),
+                     "traffic": PREFILL_TRAFFIC_BYTES, "kernel_ms": round(attn_ms, 4),
                      "algorithmic_flops": flops},
         "fused_norm_rope_kv": {"bound": "hbm", "ms": round(fused_ms, 4),
                                "gbs": round(fused_bytes(S) / (fused_ms * 1e-3) / 1e9, 1),
                                "frac": round(fused_bytes(S) / (fused_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
                                "algorithmic_bytes": fused_bytes(S)},
-        "e2e": {"value": round(world * flops * args.steps / (e2e_ms * 1e-3) / 1e12, 2),
+        "e2e": {"value": round(job_tflops(flops, args.steps, world, e2e_ms), 2),
                 "unit": "TFLOP/s", "h2d_bytes_per_step": int(hq_.numel() * 2 + hk_.numel() * 2 + hv_.numel() * 2),
                 "d2h_bytes_per_step": int(host_out.numel() * 2),
                 "ms_per_step": round(e2e_ms / args.steps, 4),
@@ -280,6 +325,9 @@ def decode_grid(args, dev, pk):
     cells = []
     shapes = [(1, 32, 8, 1024)] + [(B, 64, 8, L) for B in (1, 8, 32, 64)
                                    for L in (2048, 8192, 16384, 32768)]
+    if args.decode_cells:
+        shapes = [(int(b), 64, 8, int(l)) for b, l in
+                  (c.split("x") for c in args.decode_cells.split(","))]
     reps = max(3, min(args.steps, 10))
     for B, hq, hkv, L in shapes:
         kc = torch.randn(B, hkv, L, D, device=dev, dtype=torch.float16)
@@ -289,14 +337,13 @@ def decode_grid(args, dev, pk):
         pos = torch.full((B,), L - 1, dtype=torch.int32, device=dev)
         nks = g.decode_splits(B, L, hq, hkv, L)
         ws = torch.empty(max(16, g.decode_workspace_bytes(B, L, hq, hkv, L)), dtype=torch.uint8, device=dev)
-        for _ in range(3):
-            g.attention_decode(q, kc, vc, pos, out, L, workspace=ws)
+        graph = capture(lambda: g.attention_decode(q, kc, vc, pos, out, L, workspace=ws))
         ts = []
         for _ in range(reps):
             flush.fill_(1.0)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            g.attention_decode(q, kc, vc, pos, out, L, workspace=ws)
+            graph.replay()
             e1.record()
             torch.cuda.synchronize()
             ts.append(e0.elapsed_time(e1))
@@ -317,14 +364,13 @@ def decode_grid(args, dev, pk):
 def run_reference(args):
     """The reference's CPU path for the same workload (the oracle port; the
     Rust reference cannot be built here), all host threads, K timed steps
-    each on the bounded sample."""
+    each on the bounded sample (about 5 s of CPU work per step)."""
     import oracle
-    for _ in range(args.warmup):
-        pass
+    cpu_baseline(rows_step=512)  # warm-up: page in, spin up the thread pool
     vals = []
     last = None
     for _ in range(args.steps):
-        last = cpu_baseline(rows_step=256)
+        last = cpu_baseline(rows_step=4)
         vals.append(last["value"])
     v = statistics.median(vals)
     return {"metric": METRIC, "value": round(v, 6), "unit": "TFLOP/s", "impl": "reference",
@@ -348,6 +394,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the prefill workload (decode grid only; for profiling)")
+    ap.add_argument("--decode-cells", default="",
+                    help="comma list BxL of config-3 cells (default: the full grid + config 1)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank = int(os.environ.get("RANK", "0"))
@@ -364,7 +414,15 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
-    line = run_ours(args, rank, world, local_rank)
+    if args.no_prefill:
+        import torch
+        import grout_b200 as g
+        dev = torch.device("cuda", local_rank)
+        torch.cuda.set_device(dev)
+        g.init(local_rank)
+        line = {"decode": decode_grid(args, dev, peaks())} if rank == 0 else None
+    else:
+        line = run_ours(args, rank, world, local_rank)
     if line is not None:
         print(json.dumps(line), flush=True)
     if world > 1:
