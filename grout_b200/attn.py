@@ -96,6 +96,9 @@ SIGNATURES = {
                                          _vp, _sz, _vp]),
     "grout_attn_decode_ex": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i32, _i32, _i32,
                                             _DIMS, _vp, _sz, _vp]),
+    "grout_attn_decode_noalloc_max_bytes": (_sz, []),
+    "grout_attn_decode_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i32, _i32,
+                                                 _DIMS, _vp]),
 }
 
 _lib = None
@@ -321,6 +324,31 @@ def attention_decode(q, k_cache, v_cache, position, out, max_kv_len, workspace=N
         _ptr(q), _ptr(k_cache), _ptr(v_cache), hkv * max_seq * HEAD_DIM, max_seq * HEAD_DIM,
         _ptr(position), _ptr(out), B, int(max_kv_len), int(num_splits), ctypes.byref(dims),
         _ptr(workspace), ws_bytes, _stream(q)))
+    return out
+
+
+def attention_decode_noalloc(q, k_cache, v_cache, position, out, max_kv_len, qk_scale=None,
+                             scale_f16=True):
+    """attention_decode without a workspace, for callers that cannot allocate
+    device memory (a fixed memory plan, an FFI host with no allocator, code
+    inside a stream capture).  The split-K scratch is the library's own
+    fixed device array (grout_attn_decode_noalloc_max_bytes(), 8 MiB); larger
+    shapes raise GroutError.  Calls that can overlap on the GPU share that
+    array and race; make the first call on a device before any capture."""
+    for t, n in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache"), (out, "out")):
+        _f16_cuda(t, n)
+    B = q.shape[0] if q.dim() == 3 else 1
+    hq = q.shape[-2]
+    kc = k_cache if k_cache.dim() == 4 else k_cache.unsqueeze(0)
+    _need(v_cache.shape == k_cache.shape and out.shape == q.shape, "shape mismatch")
+    _need(position.is_cuda and position.dtype in (torch.int32, torch.uint32) and position.numel() >= B,
+          "position must be a device int32/uint32 tensor with one entry per sequence")
+    hkv, max_seq = kc.shape[1], kc.shape[2]
+    dims = make_dims(hq, hkv, max_seq, qk_scale=qk_scale,
+                     flags=FLAG_DECODE_SCALE_F16 if scale_f16 else 0)
+    _check(lib().grout_attn_decode_noalloc(
+        _ptr(q), _ptr(k_cache), _ptr(v_cache), hkv * max_seq * HEAD_DIM, max_seq * HEAD_DIM,
+        _ptr(position), _ptr(out), B, int(max_kv_len), ctypes.byref(dims), _stream(q)))
     return out
 
 

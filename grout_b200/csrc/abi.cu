@@ -132,6 +132,9 @@ int choose_splits(int32_t batch, int32_t max_kv_len, int32_t hkv, int num_sms) {
 }
 
 }  // namespace
+
+void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+
 }  // namespace grout
 
 using namespace grout;

@@ -9,6 +9,9 @@ namespace grout {
 
 constexpr int kHeadDim = 128;
 
+// Sets the message grout_attn_last_error() returns on this thread.
+void set_last_error(const char* msg);
+
 struct NormRopeArgs {
   const __half* q;     // prefill: q rows; decode: qkv rows
   const __half* k;     // prefill only

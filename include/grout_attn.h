@@ -212,6 +212,26 @@ grout_status grout_attn_decode_ex(const void* q, const void* k_cache, const void
                                   const grout_attn_dims* dims, void* workspace,
                                   size_t workspace_bytes, grout_stream_t stream);
 
+/* Allocation-free decode.  No counterpart in the reference.  For callers that
+ * cannot provide a device workspace — an engine whose device memory is all
+ * owned by a planner, an FFI host without a device allocator, code already
+ * inside a stream capture.  Same arguments and result as grout_attn_decode
+ * without the workspace: the split-K scratch lives in a fixed array in the
+ * library's device memory (grout_attn_decode_noalloc_max_bytes() = 8 MiB,
+ * held on every GPU that loads the library until the process exits).  A
+ * shape whose scratch (grout_attn_decode_workspace_bytes) exceeds that is
+ * rejected with GROUT_ERR_INVALID_ARG.  The first call on a device resolves
+ * the array's device address (the device must be current); make that first
+ * call before any stream capture.  All calls on a device share the array:
+ * calls that can overlap on the GPU (unordered streams) race; ordered calls
+ * are safe.  Allocates nothing, ever. */
+size_t grout_attn_decode_noalloc_max_bytes(void);
+grout_status grout_attn_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                       int64_t cache_batch_stride, int64_t cache_head_stride,
+                                       const uint32_t* d_position, void* out, int32_t batch,
+                                       int32_t max_kv_len, const grout_attn_dims* dims,
+                                       grout_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
