@@ -36,7 +36,7 @@ constexpr int kThreads = 160;
 constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
 
 struct RedSmem {
-  float o[4][128][8];
+  float o[4][128][9];  // padded: the per-dimension merge reads are conflict-free
   float m[4][8];
   float l[4][8];
 };

@@ -4,46 +4,55 @@
 // (reference src/kernels.rs:4845-5168, 5180-5452).  HBM-bound: every byte of
 // q/k/v is read once and every output byte written once.
 //
-// Mapping: one half-warp (16 lanes) per 128-element head row.  Lane j owns
-// the RoPE pairs i = 4j..4j+3, i.e. x[4j..4j+4) ("lo") and x[64+4j..64+4j+4)
-// ("hi"), so rotate-half needs no shuffle and each half-warp load instruction
-// covers two 128-byte segments.  The arithmetic is pinned so that the CPU
-// oracle reproduces it bit for bit: no FMA contraction (explicit _rn
-// intrinsics), a fixed sum order (lane sum (t0+t1)+(t2+t3), then a
-// xor-butterfly 8,4,2,1), rsqrt as 1/sqrt with IEEE rounding, and cos/sin
-// read from a table of correctly rounded values of the reference's f32 angle.
+// Mapping: one octet (8 lanes) per 128-element head row, so a warp works on
+// four rows at once.  Lane j of the octet owns the RoPE pairs i = 8j..8j+7,
+// i.e. x[8j..8j+8) ("lo") and x[64+8j..64+8j+8) ("hi"): rotate-half needs no
+// shuffle, every access is 16 bytes per lane, and an octet's load covers two
+// 128-byte segments.  The arithmetic is pinned so that the CPU oracle
+// reproduces it bit for bit: no FMA contraction (explicit _rn intrinsics), a
+// fixed sum order (lane sum ((t0+t1)+(t2+t3))+((t4+t5)+(t6+t7)), then a
+// xor-butterfly 4,2,1), rsqrt as a correctly rounded reciprocal of a
+// correctly rounded sqrt, and cos/sin read from a table of correctly rounded
+// values of the reference's f32 angle.
 #include "internal.h"
 #include "ptx.cuh"
 
 namespace grout {
 
-__device__ __forceinline__ void ld_half4(const __half* p, float (&f)[4]) {
-  uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
-  __half2 a = *reinterpret_cast<__half2*>(&u.x);
-  __half2 b = *reinterpret_cast<__half2*>(&u.y);
-  float2 fa = __half22float2(a), fb = __half22float2(b);
-  f[0] = fa.x; f[1] = fa.y; f[2] = fb.x; f[3] = fb.y;
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+    float2 v = __half22float2(h);
+    f[2 * i] = v.x;
+    f[2 * i + 1] = v.y;
+  }
 }
 
-__device__ __forceinline__ void st_half4(__half* p, const float (&f)[4]) {
-  __half2 a = __halves2half2(__float2half_rn(f[0]), __float2half_rn(f[1]));
-  __half2 b = __halves2half2(__float2half_rn(f[2]), __float2half_rn(f[3]));
-  uint2 u;
-  u.x = *reinterpret_cast<uint32_t*>(&a);
-  u.y = *reinterpret_cast<uint32_t*>(&b);
-  *reinterpret_cast<uint2*>(p) = u;
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ uint4 ldg16(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
 }
 
 __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const NormRopeArgs a) {
-  const int j = threadIdx.x & 15;  // lane within the half-warp
-  const unsigned mask = 0xFFFFu << (threadIdx.x & 16);
-  const int heads = a.hq + a.hkv;
-  const int64_t ntask = (int64_t)a.rows * heads;
-  const int64_t step = ((int64_t)gridDim.x * blockDim.x) >> 4;
-  for (int64_t task = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4; task < ntask;
-       task += step) {
-    const int s = (int)(task / heads);
-    const int hh = (int)(task - (int64_t)s * heads);
+  const int j = threadIdx.x & 7;  // lane within the octet
+  const unsigned mask = 0xFFu << (threadIdx.x & 24);
+  const uint32_t heads = (uint32_t)(a.hq + a.hkv);
+  const uint32_t ntask = (uint32_t)a.rows * heads;
+  const uint32_t step = (gridDim.x * blockDim.x) >> 3;
+  for (uint32_t task = (blockIdx.x * blockDim.x + threadIdx.x) >> 3; task < ntask; task += step) {
+    const uint32_t s = task / heads;
+    const int hh = (int)(task - s * heads);
     const bool is_q = hh < a.hq;
     const int kh = hh - a.hq;
     const __half* src;
@@ -80,49 +89,62 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const NormRopeArgs
         vdst = a.v_cache + off;
       }
     }
-    // V: verbatim copy, issued first so it overlaps the norm math.
+    // Issue every load of the row first.
+    const uint4 xl = ldg16(src + 8 * j);
+    const uint4 xh = ldg16(src + 64 + 8 * j);
+    uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
     if (vsrc) {
-      const uint2 v0 = __ldg(reinterpret_cast<const uint2*>(vsrc + 4 * j));
-      const uint2 v1 = __ldg(reinterpret_cast<const uint2*>(vsrc + 64 + 4 * j));
-      *reinterpret_cast<uint2*>(vdst + 4 * j) = v0;
-      *reinterpret_cast<uint2*>(vdst + 64 + 4 * j) = v1;
+      v0 = ldg16(vsrc + 8 * j);
+      v1 = ldg16(vsrc + 64 + 8 * j);
     }
-    float lo[4], hi[4], wl[4], wh[4];
-    ld_half4(src + 4 * j, lo);
-    ld_half4(src + 64 + 4 * j, hi);
     const __half* w = is_q ? a.q_w : a.k_w;
-    ld_half4(w + 4 * j, wl);
-    ld_half4(w + 64 + 4 * j, wh);
-    const float4 c4 = __ldg(reinterpret_cast<const float4*>(a.table + pos * kHeadDim + 4 * j));
-    const float4 s4 = __ldg(reinterpret_cast<const float4*>(a.table + pos * kHeadDim + 64 + 4 * j));
-    const float cs[4] = {c4.x, c4.y, c4.z, c4.w};
-    const float sn[4] = {s4.x, s4.y, s4.z, s4.w};
+    const uint4 wl4 = ldg16(w + 8 * j);
+    const uint4 wh4 = ldg16(w + 64 + 8 * j);
+    const float* trow = a.table + pos * kHeadDim;
+    const float4 c0 = __ldg(reinterpret_cast<const float4*>(trow + 8 * j));
+    const float4 c1 = __ldg(reinterpret_cast<const float4*>(trow + 8 * j + 4));
+    const float4 s0 = __ldg(reinterpret_cast<const float4*>(trow + 64 + 8 * j));
+    const float4 s1 = __ldg(reinterpret_cast<const float4*>(trow + 64 + 8 * j + 4));
+    if (vsrc) {  // V: verbatim copy
+      *reinterpret_cast<uint4*>(vdst + 8 * j) = v0;
+      *reinterpret_cast<uint4*>(vdst + 64 + 8 * j) = v1;
+    }
+    float lo[8], hi[8], wl[8], wh[8];
+    unpack8(xl, lo);
+    unpack8(xh, hi);
+    unpack8(wl4, wl);
+    unpack8(wh4, wh);
+    const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 
-    float t[4];
+    float t[8];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) t[e] = __fadd_rn(__fmul_rn(lo[e], lo[e]), __fmul_rn(hi[e], hi[e]));
-    float ss = __fadd_rn(__fadd_rn(t[0], t[1]), __fadd_rn(t[2], t[3]));
+    for (int e = 0; e < 8; ++e) t[e] = __fadd_rn(__fmul_rn(lo[e], lo[e]), __fmul_rn(hi[e], hi[e]));
+    float ss = __fadd_rn(__fadd_rn(__fadd_rn(t[0], t[1]), __fadd_rn(t[2], t[3])),
+                         __fadd_rn(__fadd_rn(t[4], t[5]), __fadd_rn(t[6], t[7])));
 #pragma unroll
-    for (int off = 8; off >= 1; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(mask, ss, off, 16));
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), a.eps)));
+    for (int off = 4; off >= 1; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(mask, ss, off, 8));
+    // ss / 128 is an exact power-of-two scaling; the correctly rounded
+    // reciprocal equals the IEEE quotient 1.0f / x.
+    const float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(ss, 0.0078125f), a.eps)));
 
-    float ylo[4], yhi[4];
+    float ylo[8], yhi[8];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
+    for (int e = 0; e < 8; ++e) {
       const float nlo = __fmul_rn(__fmul_rn(lo[e], inv), wl[e]);
       const float nhi = __fmul_rn(__fmul_rn(hi[e], inv), wh[e]);
       ylo[e] = __fsub_rn(__fmul_rn(nlo, cs[e]), __fmul_rn(nhi, sn[e]));
       yhi[e] = __fadd_rn(__fmul_rn(nhi, cs[e]), __fmul_rn(nlo, sn[e]));
     }
-    st_half4(dst + 4 * j, ylo);
-    st_half4(dst + 64 + 4 * j, yhi);
+    *reinterpret_cast<uint4*>(dst + 8 * j) = pack8(ylo);
+    *reinterpret_cast<uint4*>(dst + 64 + 8 * j) = pack8(yhi);
   }
 }
 
 cudaError_t launch_qk_norm_rope_kv(const NormRopeArgs& a, int num_sms, cudaStream_t s) {
   const int64_t ntask = (int64_t)a.rows * (a.hq + a.hkv);
   if (ntask == 0) return cudaSuccess;
-  const int per_block = 256 / 16;
+  const int per_block = 256 / 8;
   int64_t blocks = (ntask + per_block - 1) / per_block;
   const int64_t cap = (int64_t)num_sms * 8;  // 8 resident 256-thread blocks per SM
   if (blocks > cap) blocks = cap;

@@ -17,7 +17,7 @@
 // by an independent numpy restatement (tests/golden/gen_golden.py).
 //
 // Every function names the reference file:line it follows.  Build:
-// oracle/build.py (g++ -O3 -march=native -fopenmp -ffp-contract=off).
+// oracle/build.py (g++ -O3 -march=x86-64-v2 -fopenmp -ffp-contract=off).
 // -ffp-contract=off matters: the bit-exact fused norm/RoPE oracle must not
 // be contracted into FMAs.
 
@@ -132,30 +132,31 @@ void oracle_rope_table(const float* inv_freq, int32_t half, int32_t max_seq, flo
 //   ss  = sum(x_lo^2 + x_hi^2);  inv = rsqrt(ss / D + eps)
 //   n   = (x * inv) * w
 //   y_lo = n_lo*cos - n_hi*sin ;  y_hi = n_hi*cos + n_lo*sin ; one f16 rounding
-// Summation order (our contract, shared with the CUDA kernel): 16 lanes, lane
-// j owns x[4j..4j+4) and x[64+4j..64+4j+4); t_e = lo_e^2 + hi_e^2;
-// lane sum = (t0+t1)+(t2+t3); then a xor-butterfly over the 16 lanes with
-// offsets 8,4,2,1.  rsqrt is evaluated as 1/sqrt with IEEE rounding.
+// Summation order (our contract, shared with the CUDA kernel): 8 lanes, lane
+// j owns x[8j..8j+8) and x[64+8j..64+8j+8); t_e = lo_e^2 + hi_e^2;
+// lane sum = ((t0+t1)+(t2+t3)) + ((t4+t5)+(t6+t7)); then a xor-butterfly over
+// the 8 lanes with offsets 4,2,1.  rsqrt is evaluated as 1/sqrt with IEEE
+// rounding; ss / 128 is exact scaling.
 static void norm_rope_row(const u16* x, const u16* w, const float* cs, const float* sn,
                           float eps, u16* y) {
   float xf[128];
   for (int i = 0; i < 128; ++i) xf[i] = h2f(x[i]);
-  float s[16];
-  for (int j = 0; j < 16; ++j) {
-    float t[4];
-    for (int e = 0; e < 4; ++e) {
-      int i = 4 * j + e;
+  float s[8];
+  for (int j = 0; j < 8; ++j) {
+    float t[8];
+    for (int e = 0; e < 8; ++e) {
+      int i = 8 * j + e;
       float a = xf[i] * xf[i];
       float b = xf[64 + i] * xf[64 + i];
       t[e] = a + b;
     }
-    float u = t[0] + t[1];
-    float v = t[2] + t[3];
-    s[j] = u + v;
+    float u0 = t[0] + t[1], u1 = t[2] + t[3], u2 = t[4] + t[5], u3 = t[6] + t[7];
+    float v0 = u0 + u1, v1 = u2 + u3;
+    s[j] = v0 + v1;
   }
-  for (int off = 8; off >= 1; off >>= 1) {
-    float s2[16];
-    for (int j = 0; j < 16; ++j) s2[j] = s[j] + s[j ^ off];
+  for (int off = 4; off >= 1; off >>= 1) {
+    float s2[8];
+    for (int j = 0; j < 8; ++j) s2[j] = s[j] + s[j ^ off];
     std::memcpy(s, s2, sizeof(s));
   }
   float ss = s[0];

@@ -5,8 +5,9 @@ shared with oracle/ or grout_b200/) of the reference math, on small seeded
 inputs:
   - build_inv_freq (src/model.rs:7295-7306) and the RoPE angle table;
   - the fused Q/K RMSNorm + RoPE + KV write (src/kernels.rs:5012-5166) with
-    the summation order the CUDA kernel and the C++ oracle share (16 lanes of
-    4 lo + 4 hi elements, lane sum (t0+t1)+(t2+t3), xor butterfly 8,4,2,1);
+    the summation order the CUDA kernel and the C++ oracle share (8 lanes of
+    8 lo + 8 hi elements, lane sum ((t0+t1)+(t2+t3))+((t4+t5)+(t6+t7)), xor
+    butterfly 4,2,1);
   - causal GQA prefill attention and GQA decode attention, in float64
     (the "ideal" result the f16 kernels are held to within tolerance);
   - the reference's microbench KAT pattern (attention_microbench.rs:203-214).
@@ -66,11 +67,11 @@ def rope_table(inv, max_seq):
 def norm_rope_row(x16, w16, cs, sn, eps):
     x = x16.astype(np.float32)
     w = w16.astype(np.float32)
-    lo, hi = x[:64].reshape(16, 4), x[64:].reshape(16, 4)
+    lo, hi = x[:64].reshape(8, 8), x[64:].reshape(8, 8)
     t = lo * lo + hi * hi                       # float32 elementwise
-    s = (t[:, 0] + t[:, 1]) + (t[:, 2] + t[:, 3])
-    for off in (8, 4, 2, 1):
-        s = s + s[np.arange(16) ^ off]
+    s = ((t[:, 0] + t[:, 1]) + (t[:, 2] + t[:, 3])) + ((t[:, 4] + t[:, 5]) + (t[:, 6] + t[:, 7]))
+    for off in (4, 2, 1):
+        s = s + s[np.arange(8) ^ off]
     ss = s[0]
     inv = np.float32(1.0) / np.sqrt(np.float32(ss / np.float32(128.0)) + np.float32(eps))
     nlo = (x[:64] * inv) * w[:64]
