@@ -6,12 +6,14 @@
 // f16 in, f32 accumulate, P rounded to f16 before the PV product, f16 out.
 //
 // One CTA = two 128-row query tiles of one head (256 query rows), streaming
-// 128-key K/V tiles.  Warp roles (320 threads):
+// 128-key K/V tiles.  Warp roles (384 threads, 3 warpgroups):
 //   warps 0-3  softmax for query tile 0 (one thread per query row = TMEM lane)
 //   warps 4-7  softmax for query tile 1
 //   warp 8     TMA producer: Q tiles once, then K_j, V_j into a 4-slot ring
 //   warp 9     MMA issuer (one thread): tcgen05.mma, completion via
 //              tcgen05.commit on mbarriers
+//   warps 10-11 idle (they complete the third warpgroup, whose registers
+//              setmaxnreg hands to the softmax warpgroups)
 // Tensor memory (512 columns, f32): S0 [0,128) S1 [128,256) O0 [256,384)
 // O1 [384,512).  P_t (f16 pairs) overwrites the first 64 columns of S_t and
 // feeds the PV MMA straight from TMEM (A operand in TMEM, V from shared
@@ -36,7 +38,12 @@ constexpr int kBN = 128;          // keys per KV tile
 constexpr int kSlots = 4;         // K/V ring slots
 constexpr int kTile = 128 * 128 * 2;  // bytes of one 128x128 f16 tile (two 64-col boxes)
 constexpr int kBox = kTile / 2;
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;  // 3 warpgroups
+// Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512);
+// the producer/MMA warpgroup drops to 104, the two softmax warpgroups rise to
+// 192: 128 x 104 + 256 x 192 = 62464 <= 64512.
+constexpr int kRegsIssue = 104;
+constexpr int kRegsSoftmax = 192;
 constexpr int kOffQ = 0;                       // 2 query tiles
 constexpr int kOffKV = 2 * kTile;              // ring
 constexpr int kOffBar = kOffKV + kSlots * kTile;
@@ -50,6 +57,66 @@ constexpr int kBarS = kBarEmpty + kSlots;   // + tile
 constexpr int kBarP = kBarS + 2;            // + tile
 constexpr int kBarO = kBarP + 2;
 constexpr int kNumBars = kBarO + 1;
+
+// ---- packed f32x2 arithmetic (sm_100a): two softmax elements per instruction
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x (x <= 0) for a pair, on the FMA/ALU pipes, used for a share of the
+// softmax exponentials so the MUFU unit is not the only path.  Range
+// reduction x = n + f, n = round(x) via the 1.5*2^23 magic constant,
+// f in [-1/2, 1/2]; 2^f by a degree-3 polynomial fitted for minimum relative
+// error (max 7.6e-5, below the f16 rounding P gets next); 2^n added into the
+// exponent field.  Inputs below -125 clamp to ~2^-125 (P rounds to 0 in
+// f16); the clamp keeps n + exponent(p) >= 1, so the sum never reaches the
+// sign bit (p can be slightly below 1 when f < 0).
+__device__ __forceinline__ void ex2_poly2(uint64_t x2, float& r0, float& r1) {
+  float x0, x1;
+  f2unpack(x2, x0, x1);
+  x2 = f2pack(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const uint64_t t2 = fadd2(x2, f2pack(12582912.0f, 12582912.0f));
+  const uint64_t n2 = fadd2(t2, f2pack(-12582912.0f, -12582912.0f));
+  const uint64_t f2 = ffma2(n2, f2pack(-1.0f, -1.0f), x2);
+  uint64_t p2 = ffma2(f2pack(0.05517090484f, 0.05517090484f), f2,
+                      f2pack(0.24260953069f, 0.24260953069f));
+  p2 = ffma2(p2, f2, f2pack(0.69326096773f, 0.69326096773f));
+  p2 = ffma2(p2, f2, f2pack(0.99992817640f, 0.99992817640f));
+  float p0, p1, t0, t1;
+  f2unpack(p2, p0, p1);
+  f2unpack(t2, t0, t1);
+  r0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  r1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
+
+// Element pairs (of the 16 per 32-column chunk) whose exponentials run on
+// ex2_poly2: one in four, so MUFU carries 3/4 of the exponentials.
+__device__ __forceinline__ constexpr bool poly_pair(int i) { return (i & 3) == 3; }
+
+// Online-softmax rescaling threshold (log2 units): the reference max a row
+// exponentiates against moves only when the row max grows by more than this,
+// so P stays <= 2^8 and O is rescaled rarely.
+constexpr float kRescaleThreshold = 8.0f;
 
 __device__ __forceinline__ int ring_slot(int i) { return i % kSlots; }
 __device__ __forceinline__ uint32_t ring_parity(int i) { return (uint32_t)((i / kSlots) & 1); }
@@ -86,6 +153,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int rows_hi = min(q0 + 2 * kBM, S);
   const int kv_len = P + S;
   const int n_kv = (P + rows_hi + kBN - 1) / kBN;
+  // query tile 0 (rows q0 .. q0+127) never sees keys beyond P + q0 + 127
+  const int n_kv0 = (P + min(q0 + kBM, S) + kBN - 1) / kBN;
   const int kh = h / (a.hq / a.hkv);
   const int kvb = a.kv_batched ? b : 0;
 
@@ -108,6 +177,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_holder;
   const uint32_t smem_base = smem_u32(smem);
 
+  if (warp >= 8) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsIssue));
   if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -147,15 +218,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_f16_f32(kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = idesc_f16_f32(kBM, 128, 0, 1);
-      const uint32_t tS[2] = {tmem + 0, tmem + 128};
-      const uint32_t tO[2] = {tmem + 256, tmem + 384};
       auto qk = [&](int t, int slot) {
         const uint32_t qa = smem_base + kOffQ + t * kTile;
         const uint32_t kb = smem_base + kOffKV + slot * kTile;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
-          tc_mma_ss(tS[t], smem_desc_sw128(qa + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024),
+          tc_mma_ss(tmem + t * 128, smem_desc_sw128(qa + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024),
                     idesc_qk, kk > 0 ? 1u : 0u);
         }
       };
@@ -163,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t vb = smem_base + kOffKV + slot * kTile;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          tc_mma_ts(tO[t], tS[t] + kk * 8, smem_desc_sw128(vb + kk * 2048, kBox, 1024), idesc_pv,
+          tc_mma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, smem_desc_sw128(vb + kk * 2048, kBox, 1024), idesc_pv,
                     (acc || kk > 0) ? 1u : 0u);
         }
       };
@@ -182,17 +251,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           const bool next = j + 1 < n_kv;
           ok = mbar_wait(smem_u32(&bars[kBarFull + ring_slot(iv)]), ring_parity(iv), a.err, 22,
                          abort_flag);
-          ok = ok && mbar_wait(smem_u32(&bars[kBarP + 0]), j & 1, a.err, 23, abort_flag);
           if (!ok) break;
-          tc_fence_after();
-          pv(0, ring_slot(iv), j > 0);
+          if (j < n_kv0) {
+            ok = mbar_wait(smem_u32(&bars[kBarP + 0]), j & 1, a.err, 23, abort_flag);
+            if (!ok) break;
+            tc_fence_after();
+            pv(0, ring_slot(iv), j > 0);
+          }
           if (next) {
             ok = mbar_wait(smem_u32(&bars[kBarFull + ring_slot(ik)]), ring_parity(ik), a.err, 24,
                            abort_flag);
             if (!ok) break;
             tc_fence_after();
-            qk(0, ring_slot(ik));
-            tc_commit(smem_u32(&bars[kBarS + 0]));
+            if (j + 1 < n_kv0) {
+              qk(0, ring_slot(ik));
+              tc_commit(smem_u32(&bars[kBarS + 0]));
+            }
           }
           ok = mbar_wait(smem_u32(&bars[kBarP + 1]), j & 1, a.err, 25, abort_flag);
           if (!ok) break;
@@ -208,7 +282,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_commit(smem_u32(&bars[kBarO]));
       }
     }
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
     // --------------------------------------------------------------- softmax
     const int t = warp >> 2;          // query tile
     const int row = threadIdx.x & 127;  // TMEM lane == query row within the tile
@@ -218,44 +294,64 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row_q = q0 + t * kBM + row;
     const int key_lim = min(P + row_q, kv_len - 1);  // last visible key
     const float sl2 = a.scale_log2;
-    float m = -INFINITY, l = 0.f;
+    const int n_t = t == 0 ? n_kv0 : n_kv;
+    float m_run = -INFINITY, l = 0.f;  // m_run: the max P is exponentiated against
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
+    for (int j = 0; j < n_t; ++j) {
       ok = mbar_wait(smem_u32(&bars[kBarS + t]), j & 1, a.err, 30 + t, abort_flag);
       if (!ok) break;
       tc_fence_after();
+      uint32_t r[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, r[c]);
+      tc_wait_ld();
       float s[128];
-      {
-        uint32_t r[32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(tS + c * 32, r);
-          tc_wait_ld();
+      for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
-        }
-      }
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[c][i]);
       const int lim = key_lim - j * kBN;
       if (lim < kBN - 1) {
 #pragma unroll
         for (int c = 0; c < 128; ++c)
           if (c > lim) s[c] = -INFINITY;
       }
-      float mx = s[0];
+      float mx0 = fmaxf(s[0], s[1]), mx1 = fmaxf(s[2], s[3]);
+      float mx2 = fmaxf(s[4], s[5]), mx3 = fmaxf(s[6], s[7]);
 #pragma unroll
-      for (int c = 1; c < 128; ++c) mx = fmaxf(mx, s[c]);
-      const float m_new = fmaxf(m, mx * sl2);
+      for (int c = 8; c < 128; c += 8) {
+        mx0 = fmax3(mx0, s[c], s[c + 1]);
+        mx1 = fmax3(mx1, s[c + 2], s[c + 3]);
+        mx2 = fmax3(mx2, s[c + 4], s[c + 5]);
+        mx3 = fmax3(mx3, s[c + 6], s[c + 7]);
+      }
+      const float mx_s = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+      float alpha = 1.0f;
+      float m_new = m_run;
+      if (mx_s > m_run + kRescaleThreshold) {
+        m_new = mx_s;
+        alpha = ex2(m_run - m_new);
+      }
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = ex2(m - m_use);
-      float rs = 0.f;
+      const uint64_t sl2x2 = f2pack(sl2, sl2);
+      const uint64_t negm2 = f2pack(-m_use, -m_use);
+      uint64_t rsum = f2pack(0.f, 0.f);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2(fmaf(s[c * 32 + 2 * i], sl2, -m_use));
-          const float p1 = ex2(fmaf(s[c * 32 + 2 * i + 1], sl2, -m_use));
-          rs += p0 + p1;
+          const uint64_t x2 = ffma2(f2pack(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1]), sl2x2, negm2);
+          float p0, p1;
+          if (poly_pair(i)) {
+            ex2_poly2(x2, p0, p1);
+          } else {
+            float x0, x1;
+            f2unpack(x2, x0, x1);
+            p0 = ex2(x0);
+            p1 = ex2(x1);
+          }
+          rsum = fadd2(rsum, f2pack(p0, p1));
           pk[i] = pack_half2(p0, p1);
         }
         asm volatile(
@@ -266,24 +362,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             "r"(pk[13]), "r"(pk[14]), "r"(pk[15])
             : "memory");
       }
-      l = l * alpha + rs;
-      // Rescale O_t when the running max moved (PV_t(j-1) has completed:
-      // it was issued before the QK that produced this S).
+      float rs0, rs1;
+      f2unpack(rsum, rs0, rs1);
+      l = l * alpha + (rs0 + rs1);
+      // Rescale O_t only when some row of the warp moved its reference max
+      // (PV_t(j-1) has completed: it was issued before the QK that produced
+      // this S).
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tO + c * 32, r);
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
           tc_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st32(tO + c * 32, r);
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tO + c * 32, o);
         }
       }
       tc_wait_st();
       tc_fence_before();
       mbar_arrive(smem_u32(&bars[kBarP + t]));
-      m = m_new;
+      m_run = m_new;
     }
     if (ok) ok = mbar_wait(smem_u32(&bars[kBarO]), 0, a.err, 40, abort_flag);
     if (ok) {
