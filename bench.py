@@ -288,6 +288,7 @@ def run_ours(args, rank, world, local_rank):
     e2e_ms = e0.elapsed_time(e1)
 
     step_ms, e2e_ms, attn_ms, fused_ms = reduce_max([step_ms, e2e_ms, attn_ms, fused_ms], dist, dev)
+    ragged = None if args.no_ragged else ragged_c4(args, dev, rank, world, dist)
     if rank != 0:
         return None
 
@@ -324,11 +325,59 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": 2 * args.steps,
         "clocks": clk.summary(),
     }
+    if ragged is not None:
+        ragged["frac"] = round(ragged["tflops"] / pk["bf16_tflops"], 4)
+        line["ragged_c4"] = ragged
     if world == 1 and not args.no_decode:
         line["decode"] = decode_grid(args, dev, pk)
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline()
     return line
+
+
+def ragged_c4(args, dev, rank, world, dist):
+    """Config 4: ragged causal prefill batch at Qwen3-8B heads (32 query / 8
+    KV heads), 16 sequences with lengths uniform in [128, 8192] (seed 5),
+    packed varlen K/V [tokens][8][128].  Across N ranks the layer is split by
+    KV head (rank r owns KV heads [r*8/N, (r+1)*8/N) and their query heads):
+    strong scaling, no collective.  FLOPs = 4*D*Hq*sum_i L_i(L_i+1)/2 for the
+    whole batch; time = max over ranks of the per-rank kernel time."""
+    import torch
+    import grout_b200 as g
+    from grout_b200 import synth
+    hq, hkv = 32, 8
+    lens = synth.ragged_lengths(5, 16, 128, 8192)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    tot = int(cu[-1])
+    gen = torch.Generator(device=dev).manual_seed(5)
+    q = torch.randn(tot, hq, D, device=dev, generator=gen).half()
+    k = torch.randn(tot, hkv, D, device=dev, generator=gen).half()
+    v = torch.randn(tot, hkv, D, device=dev, generator=gen).half()
+    out = torch.empty_like(q)
+    dcu = torch.from_numpy(cu).to(dev)
+    ks = dcu[:-1].contiguous()
+    lo, hi = shard_kv_heads(hkv, world, rank)
+    graph = capture(lambda: g.attention_prefill_varlen(
+        q, k, v, out, dcu, int(lens.max()), hkv, kv_row_stride=hkv * D, kv_head_stride=D,
+        kv_rows=tot, kv_start=ks, kv_head_range=(lo, hi)))
+    flush = L2Flush(dev)
+    ts = []
+    for _ in range(max(3, min(args.steps, 10))):
+        flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    g.check_device_error()
+    (ms,) = reduce_max([statistics.median(ts)], dist, dev)
+    flops = 4.0 * D * hq * float(np.sum(lens.astype(np.float64) * (lens + 1) / 2))
+    return {"workload": "C4: 16 ragged sequences, L ~ U[128, 8192] (seed 5), Qwen3-8B heads 32/8",
+            "tokens": tot, "lengths": lens.tolist(), "ms": round(ms, 4),
+            "tflops": round(flops / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+            "sharding": f"KV heads split over {world} rank(s), strong scaling",
+            "algorithmic_flops": flops}
 
 
 def decode_grid(args, dev, pk):
@@ -411,6 +460,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-ragged", action="store_true", help="skip the config-4 ragged batch")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the prefill workload (decode grid only; for profiling)")
     ap.add_argument("--decode-cells", default="",

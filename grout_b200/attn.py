@@ -261,23 +261,36 @@ def attention_prefill(q, k_cache, v_cache, out, position_start=0, qk_scale=None)
 
 def attention_prefill_varlen(q, k, v, out, cu_seqlens_q, max_q_len, num_kv_heads,
                              kv_row_stride, kv_head_stride, kv_batch_stride=0, kv_rows=None,
-                             position_start=None, kv_start=None, qk_scale=None):
+                             position_start=None, kv_start=None, qk_scale=None,
+                             kv_head_range=None):
     """Packed varlen causal prefill.  q, out [q_rows, Hq, 128]; k/v addressed
     by element strides (see grout_prefill_varlen_args); cu_seqlens_q,
-    position_start, kv_start: device int32."""
+    position_start, kv_start: device int32.
+
+    kv_head_range=(lo, hi) computes only KV heads lo..hi-1 and their query
+    heads (the shard one GPU owns when a layer is split by KV head); the
+    tensors stay whole, the call addresses the shard in place."""
     for t, n in ((q, "q"), (k, "k"), (v, "v"), (out, "out")):
         _f16_cuda(t, n)
     _need(cu_seqlens_q.is_cuda and cu_seqlens_q.dtype == torch.int32, "cu_seqlens_q must be device int32")
+    _need(out.shape == q.shape, "out shape mismatch")
     B = cu_seqlens_q.numel() - 1
     hq = q.shape[1]
+    _need(hq % num_kv_heads == 0, f"{hq} query heads do not group over {num_kv_heads} KV heads")
+    G = hq // num_kv_heads
     if kv_rows is None:
         kv_rows = (k.numel() - (B - 1) * kv_batch_stride) // max(1, kv_row_stride) if kv_batch_stride else k.numel() // kv_row_stride
+    lo, hi = kv_head_range if kv_head_range is not None else (0, num_kv_heads)
+    _need(0 <= lo < hi <= num_kv_heads, f"kv_head_range {kv_head_range} outside 0..{num_kv_heads}")
+    qoff = lo * G * HEAD_DIM * 2            # bytes
+    kvoff = lo * kv_head_stride * 2
     args = PrefillVarlenArgs(
-        q.data_ptr(), out.data_ptr(), hq * HEAD_DIM, q.shape[0], k.data_ptr(), v.data_ptr(),
+        q.data_ptr() + qoff, out.data_ptr() + qoff, hq * HEAD_DIM, q.shape[0],
+        k.data_ptr() + kvoff, v.data_ptr() + kvoff,
         kv_batch_stride, kv_row_stride, kv_head_stride, int(kv_rows), cu_seqlens_q.data_ptr(),
         position_start.data_ptr() if position_start is not None else None,
         kv_start.data_ptr() if kv_start is not None else None, B, int(max_q_len))
-    dims = make_dims(hq, num_kv_heads, 1 << 30, qk_scale=qk_scale)
+    dims = make_dims((hi - lo) * G, hi - lo, 1 << 30, qk_scale=qk_scale)
     _check(lib().grout_attn_prefill_varlen(ctypes.byref(args), ctypes.byref(dims), _stream(q)))
     return out
 

@@ -130,3 +130,28 @@ def test_prefill_config2_full_size_sampled_rows(grout):
     out, ref = _engine_case(grout, S, hq, hkv, 0, S, seed=5, rows_step=61)
     rows = np.arange(0, S, 61)
     _check(out, ref, rows=rows)
+
+
+def test_prefill_kv_head_shards_are_bitwise_identical(grout):
+    """Config 4 sharding: each KV-head shard (what one GPU of 2/4/8 computes)
+    reproduces its rows of the unsharded launch bit for bit."""
+    hq, hkv = 32, 8
+    lens = synth.ragged_lengths(5, 5, 128, 700)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    tot = int(cu[-1])
+    q = _dev(synth.normal(61, tot * hq * D).reshape(tot, hq, D))
+    k = _dev(synth.normal(62, tot * hkv * D).reshape(tot, hkv, D))
+    v = _dev(synth.normal(63, tot * hkv * D).reshape(tot, hkv, D))
+    dcu = _dev(cu)
+    kw = dict(kv_row_stride=hkv * D, kv_head_stride=D, kv_rows=tot, kv_start=dcu[:-1].contiguous())
+    full = torch.zeros(tot, hq, D, dtype=torch.float16, device="cuda:0")
+    grout.attention_prefill_varlen(q, k, v, full, dcu, int(lens.max()), hkv, **kw)
+    for world in (2, 4, 8):
+        shard = torch.zeros_like(full)
+        per = hkv // world
+        for r in range(world):
+            grout.attention_prefill_varlen(q, k, v, shard, dcu, int(lens.max()), hkv,
+                                           kv_head_range=(r * per, (r + 1) * per), **kw)
+        torch.cuda.synchronize()
+        assert torch.equal(shard.view(torch.int16), full.view(torch.int16)), world
+    grout.check_device_error()
