@@ -477,6 +477,9 @@ def main():
         return
 
     if world > 1:
+        # keep NCCL's version banner off stdout: the JSON line must be alone
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
