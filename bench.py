@@ -289,6 +289,7 @@ def run_ours(args, rank, world, local_rank):
 
     step_ms, e2e_ms, attn_ms, fused_ms = reduce_max([step_ms, e2e_ms, attn_ms, fused_ms], dist, dev)
     ragged = None if args.no_ragged else ragged_c4(args, dev, rank, world, dist)
+    c5 = None if args.no_e2e_decode else config5(args, rank, world, dist)
     if rank != 0:
         return None
 
@@ -328,11 +329,46 @@ def run_ours(args, rank, world, local_rank):
     if ragged is not None:
         ragged["frac"] = round(ragged["tflops"] / pk["bf16_tflops"], 4)
         line["ragged_c4"] = ragged
+    if c5 is not None:
+        line["e2e_decode_c5"] = c5
     if world == 1 and not args.no_decode:
         line["decode"] = decode_grid(args, dev, pk)
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline()
     return line
+
+
+def config5(args, rank, world, dist):
+    """Config 5: Qwen3-32B greedy decode (random f16 weights), 8192-token
+    prompt then 256 tokens under CUDA-graph replay, tensor-parallel over the
+    N ranks (NCCL all-reduce after o_proj / down_proj).  Roofline tok/s =
+    measured HBM GB/s / bytes each rank reads per token (its weight shard +
+    its KV cache at the final position)."""
+    import torch
+    from grout_b200 import qwen3_tp
+    c = qwen3_tp.Qwen3Shape()
+    r = qwen3_tp.run_config5(rank, world, None, prompt_len=args.c5_prompt,
+                             gen_tokens=args.c5_tokens, shape=c,
+                             barrier=dist.barrier if dist else None)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    vals = reduce_max([r["decode_ms"], r["prefill_ms"], r["attn_ms_per_step"]], dist, dev)
+    decode_ms, prefill_ms, attn_ms = vals
+    torch.cuda.empty_cache()
+    D, H = c.head_dim, c.hidden
+    per_layer = (c.heads + 2 * c.kv_heads) * D * H + H * c.heads * D + 3 * H * c.inter
+    w_bytes = 2.0 * (c.layers * per_layer + c.vocab * H) / world
+    kv_bytes = 2.0 * c.layers * 2 * (c.kv_heads // world) * (args.c5_prompt + args.c5_tokens) * D
+    step_ms = decode_ms / args.c5_tokens
+    hbm = peaks()["hbm_gbs"]
+    roof = hbm * 1e9 / (w_bytes + kv_bytes)
+    return {"workload": f"C5: Qwen3-32B greedy decode, prompt {args.c5_prompt}, "
+                        f"{args.c5_tokens} tokens, TP={world}, CUDA-graph replay",
+            "tok_s": round(args.c5_tokens / (decode_ms * 1e-3), 2), "ms_per_token": round(step_ms, 4),
+            "prefill_ms": round(prefill_ms, 2),
+            "attention_ms_per_token": round(attn_ms, 4),
+            "attention_share": round(attn_ms / step_ms, 4),
+            "roofline_tok_s": round(roof, 1), "frac": round(args.c5_tokens / (decode_ms * 1e-3) / roof, 4),
+            "bytes_per_token_per_rank": w_bytes + kv_bytes, "first_tokens": r["first_tokens"]}
 
 
 def ragged_c4(args, dev, rank, world, dist):
@@ -461,6 +497,9 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ragged", action="store_true", help="skip the config-4 ragged batch")
+    ap.add_argument("--no-e2e-decode", action="store_true", help="skip config 5 (Qwen3-32B decode)")
+    ap.add_argument("--c5-prompt", type=int, default=8192)
+    ap.add_argument("--c5-tokens", type=int, default=256)
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the prefill workload (decode grid only; for profiling)")
     ap.add_argument("--decode-cells", default="",
