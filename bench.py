@@ -169,6 +169,7 @@ def cpu_baseline(rows_step=2):
     all 64 heads.  TFLOP/s = attention FLOPs of the sampled rows / time of
     (sampled attention + fused write scaled to the same row fraction)."""
     import oracle
+    oracle.set_num_threads(os.cpu_count() or 1)
     q, k, v, qw, kw = make_inputs(0)
     tab = oracle.rope_table(oracle.inv_freq(THETA, D), S)
     kc = np.zeros((HKV, S, D), np.float16)
@@ -468,6 +469,7 @@ def run_reference(args):
     Rust reference cannot be built here), all host threads, K timed steps
     each on the bounded sample (about 5 s of CPU work per step)."""
     import oracle
+    oracle.set_num_threads(os.cpu_count() or 1)  # torchrun sets OMP_NUM_THREADS=1
     cpu_baseline(rows_step=512)  # warm-up: page in, spin up the thread pool
     vals = []
     last = None
@@ -488,7 +490,22 @@ def run_reference(args):
                     "d2h_bytes_per_step": 0}}
 
 
+def emit(line):
+    """Writes the one JSON line to the real stdout (see main)."""
+    os.write(_STDOUT_FD, (json.dumps(line) + "\n").encode())
+
+
+_STDOUT_FD = 1
+
+
 def main():
+    # Everything else that reaches fd 1 (e.g. the NCCL version banner printed
+    # when a communicator is created) goes to stderr: stdout carries only the
+    # JSON line.
+    global _STDOUT_FD
+    sys.stdout.flush()
+    _STDOUT_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
@@ -512,13 +529,10 @@ def main():
 
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps(run_reference(args)), flush=True)
+            emit(run_reference(args))
         return
 
     if world > 1:
-        # keep NCCL's version banner off stdout: the JSON line must be alone
-        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
-            os.environ["NCCL_DEBUG"] = "WARN"
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
@@ -533,7 +547,7 @@ def main():
     else:
         line = run_ours(args, rank, world, local_rank)
     if line is not None:
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

@@ -105,7 +105,8 @@ class Qwen3TP:
             allp = torch.empty(2 * self.world, device=self.dev, dtype=torch.float32)
             torch.distributed.all_gather_into_tensor(allp, pair, group=self.group)
             allp = allp.view(self.world, 2)
-            return allp[allp[:, 0].argmax(), 1].long().view(1)
+            best = allp[:, 0].argmax().view(1)
+            return allp[:, 1].gather(0, best).long()
         return i.view(1)
 
     # ---------------------------------------------------------------- prefill
