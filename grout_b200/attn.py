@@ -345,7 +345,7 @@ def attention_decode_noalloc(q, k_cache, v_cache, position, out, max_kv_len, qk_
     """attention_decode without a workspace, for callers that cannot allocate
     device memory (a fixed memory plan, an FFI host with no allocator, code
     inside a stream capture).  The split-K scratch is the library's own
-    fixed device array (grout_attn_decode_noalloc_max_bytes(), 8 MiB); larger
+    fixed device array (grout_attn_decode_noalloc_max_bytes(), 1 MiB); larger
     shapes raise GroutError.  Calls that can overlap on the GPU share that
     array and race; make the first call on a device before any capture."""
     for t, n in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache"), (out, "out")):

@@ -115,17 +115,17 @@ grout_status encode_map(CUtensorMap* m, const void* base, int rank, const uint64
   return GROUT_OK;
 }
 
+// Split count for decode: about one CTA per SM in total (measured on B200:
+// longer splits stream better than many short ones, and every extra split
+// costs a partial write and its share of the merge), never fewer than 256
+// keys per split.
 int choose_splits(int32_t batch, int32_t max_kv_len, int32_t hkv, int num_sms) {
   const int keys = 64;
   const int tiles = (max_kv_len + keys - 1) / keys;
-  if (tiles <= 1) return 1;
   const int64_t units = (int64_t)batch * hkv;
-  const int64_t target = (int64_t)num_sms * 2 * 4;  // about four waves at 2 CTAs per SM
-  int64_t nks = (target + units - 1) / units;
-  const int64_t lo = (tiles + 31) / 32;  // at most 2048 keys per split
-  const int64_t hi = std::max(1, tiles / 2);  // at least 128 keys per split
+  int64_t nks = (num_sms + units - 1) / units;
+  const int64_t hi = std::max(1, tiles / 4);
   if (nks > hi) nks = hi;
-  if (nks < lo) nks = lo;
   if (nks < 1) nks = 1;
   if (nks > 1024) nks = 1024;
   return (int)nks;

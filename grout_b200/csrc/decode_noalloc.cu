@@ -27,7 +27,7 @@
 
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB per device
+constexpr size_t kNoAllocScratchBytes = 1u << 20;  // 1 MiB per device
 
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 

@@ -217,7 +217,7 @@ grout_status grout_attn_decode_ex(const void* q, const void* k_cache, const void
  * owned by a planner, an FFI host without a device allocator, code already
  * inside a stream capture.  Same arguments and result as grout_attn_decode
  * without the workspace: the split-K scratch lives in a fixed array in the
- * library's device memory (grout_attn_decode_noalloc_max_bytes() = 8 MiB,
+ * library's device memory (grout_attn_decode_noalloc_max_bytes() = 1 MiB,
  * held on every GPU that loads the library until the process exits).  A
  * shape whose scratch (grout_attn_decode_workspace_bytes) exceeds that is
  * rejected with GROUT_ERR_INVALID_ARG.  The first call on a device resolves

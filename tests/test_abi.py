@@ -103,18 +103,19 @@ def test_init_without_gpu_fails_cleanly(L):
 
 
 def test_decode_split_heuristic(L):
-    """Split count: >= 1 split per 2048 keys, >= 128 keys per split, enough
-    CTAs to fill 148 SMs when the sequence allows it."""
+    """Split count: about one CTA per SM in total, at least 256 keys per
+    split, one split once the batch alone fills the GPU."""
     for B in (1, 8, 32, 64):
-        for Lk in (2048, 8192, 16384, 32768):
+        for Lk in (1024, 2048, 8192, 16384, 32768):
             n = attn.decode_splits(B, Lk, 64, 8, 32768)
             tiles = Lk // 64
-            assert 1 <= n <= max(1, tiles // 2)
-            assert Lk / n <= 2048 + 64
-            if B * 8 * tiles // 2 >= 2 * 148:
-                assert B * 8 * n >= 148
-    assert attn.decode_splits(1, 64, 64, 8, 32768) == 1
-    assert attn.decode_workspace_bytes(1, 64, 64, 8, 32768) == 0
+            assert 1 <= n <= max(1, tiles // 4)
+            assert B * 8 * (n - 1) < 148
+            if B * 8 >= 148:
+                assert n == 1
+    assert attn.decode_splits(1, 32768, 64, 8, 32768) == 19
+    assert attn.decode_splits(8, 8192, 64, 8, 32768) == 3
+    assert attn.decode_workspace_bytes(32, 8192, 64, 8, 32768) == 0
     n = attn.decode_splits(8, 8192, 64, 8, 32768)
     assert attn.decode_workspace_bytes(8, 8192, 64, 8, 32768) == 8 * 64 * n * 129 * 4
 
