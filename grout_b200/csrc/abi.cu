@@ -238,6 +238,7 @@ grout_status grout_qk_norm_rope_kv_prefill(const void* q, const void* k, const v
                                            const grout_attn_dims* dims, grout_stream_t stream) {
   grout_status st = check_dims(dims, 0);
   if (st != GROUT_OK) return st;
+  if (seq_len == 0 && position_start >= 0 && position_start <= dims->max_seq) return GROUT_OK;
   const void* ptrs[] = {q, k, v, q_norm_w, k_norm_w, rope_table, q_out, k_cache, v_cache};
   for (const void* p : ptrs) {
     if (!p) return fail(GROUT_ERR_INVALID_ARG, "null pointer argument");
@@ -290,6 +291,7 @@ grout_status grout_qk_norm_rope_kv_decode(const void* qkv, const void* q_norm_w,
                                           const grout_attn_dims* dims, grout_stream_t stream) {
   grout_status st = check_dims(dims, 0);
   if (st != GROUT_OK) return st;
+  if (batch == 0) return GROUT_OK;
   const void* ptrs[] = {qkv, q_norm_w, k_norm_w, rope_table, q_out, k_cache, v_cache, d_position};
   for (const void* p : ptrs) {
     if (!p) return fail(GROUT_ERR_INVALID_ARG, "null pointer argument");
@@ -332,6 +334,7 @@ static grout_status prefill_common(const grout_prefill_varlen_args* p, int32_t s
                                    grout_stream_t stream) {
   grout_status st = check_dims(dims, 0);
   if (st != GROUT_OK) return st;
+  if (p->batch == 0 || p->max_q_len == 0) return GROUT_OK;
   if (!p->q || !p->out || !p->k || !p->v) return fail(GROUT_ERR_INVALID_ARG, "null pointer argument");
   const void* ptrs[] = {p->q, p->out, p->k, p->v};
   for (const void* x : ptrs)
@@ -457,14 +460,14 @@ grout_status grout_attn_decode_ex(const void* q, const void* k_cache, const void
                                   size_t workspace_bytes, grout_stream_t stream) {
   grout_status st = check_dims(dims, 8);
   if (st != GROUT_OK) return st;
+  if (batch < 0) return fail(GROUT_ERR_INVALID_ARG, "batch=%d", batch);
+  if (batch == 0) return GROUT_OK;  // empty call: nothing to read or write
   const void* ptrs[] = {q, k_cache, v_cache, out};
   for (const void* p : ptrs) {
     if (!p) return fail(GROUT_ERR_INVALID_ARG, "null pointer argument");
     if (!aligned16(p)) return fail(GROUT_ERR_INVALID_ARG, "pointer %p is not 16-byte aligned", p);
   }
   if (!d_position) return fail(GROUT_ERR_INVALID_ARG, "d_position is null");
-  if (batch < 0) return fail(GROUT_ERR_INVALID_ARG, "batch=%d", batch);
-  if (batch == 0) return GROUT_OK;
   if (max_kv_len <= 0 || max_kv_len > dims->max_seq)
     return fail(GROUT_ERR_INVALID_ARG, "max_kv_len=%d must be in [1, max_seq=%d]", max_kv_len,
                 dims->max_seq);

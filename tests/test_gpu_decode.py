@@ -111,3 +111,22 @@ def test_decode_golden(grout):
     B, hkv, ms, _ = g["dc_k"].shape
     out = _run(grout, g["dc_q"], g["dc_k"], g["dc_v"], g["dc_pos"], ms)
     _check(out, g["dc_out"])
+
+
+def test_decode_position_beyond_split_hint(grout):
+    """max_kv_len only fixes the split count; a position past it (below
+    max_seq) is still attended over all its keys."""
+    B, hq, hkv, ms = 2, 64, 8, 2048
+    q, k, v = _inputs(B, hq, hkv, ms, seed=4)
+    pos = np.array([1500, 2047], np.uint32)
+    out = _run(grout, q, k, v, pos, 256)
+    ref = oracle.attn_decode(q, k, v, pos, hkv, hkv * ms * D, ms * D, SCALE_F16, nks=1, bn=64)
+    _check(out, ref)
+
+
+def test_decode_empty_batch_is_a_no_op(grout):
+    q = torch.zeros(0, 8, D, dtype=torch.float16, device="cuda:0")
+    kc = torch.zeros(1, 1, 64, D, dtype=torch.float16, device="cuda:0")
+    pos = torch.zeros(1, dtype=torch.int32, device="cuda:0")
+    grout.attention_decode(q, kc, kc.clone(), pos, q.clone(), 64)
+    torch.cuda.synchronize()

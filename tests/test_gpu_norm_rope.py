@@ -90,3 +90,30 @@ def test_decode_position_out_of_range_sets_device_error(grout):
         grout.check_device_error()
     assert kc.abs().sum().item() == 0
     grout.check_device_error()  # cleared
+
+
+def test_v_copied_bitwise_including_nan_and_inf(grout):
+    """V is copied bit for bit: arbitrary f16 bit patterns (NaN payloads,
+    infinities, subnormals) survive; the write lands at the last cache row."""
+    S, hq, hkv, ms = 3, 8, 2, 16
+    rng = np.random.default_rng(7)
+    q = synth.normal(1, S * hq * D).reshape(S, hq, D)
+    k = synth.normal(2, S * hkv * D).reshape(S, hkv, D)
+    vbits = rng.integers(0, 1 << 16, size=(S, hkv, D), dtype=np.uint16)
+    vbits[0, 0, :4] = [0x7C00, 0xFC00, 0x7E01, 0x0001]
+    v = vbits.view(np.float16)
+    w = np.ones(D, np.float16)
+    dev = torch.device("cuda", 0)
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    table = grout.rope_table(1.0e6, ms, dev)
+    kc = torch.zeros(hkv, ms, D, dtype=torch.float16, device=dev)
+    vc = torch.zeros_like(kc)
+    q_out = torch.empty(S, hq, D, dtype=torch.float16, device=dev)
+    grout.qk_norm_rope_kv_prefill(T(q), T(k), T(v), T(w), T(w), table, q_out, kc, vc, ms - S, 1e-6)
+    torch.cuda.synchronize()
+    got = vc.cpu().numpy().view(np.uint16)
+    assert np.array_equal(got[:, ms - S:].transpose(1, 0, 2), vbits)
+    assert not got[:, : ms - S].any()
+    with pytest.raises(grout.GroutError, match="exceeds max_seq"):
+        grout.qk_norm_rope_kv_prefill(T(q), T(k), T(v), T(w), T(w), table, q_out, kc, vc,
+                                      ms - S + 1, 1e-6)

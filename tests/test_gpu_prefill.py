@@ -155,3 +155,18 @@ def test_prefill_kv_head_shards_are_bitwise_identical(grout):
         torch.cuda.synchronize()
         assert torch.equal(shard.view(torch.int16), full.view(torch.int16)), world
     grout.check_device_error()
+
+
+@pytest.mark.parametrize("S,P", [(127, 0), (129, 0), (255, 1), (256, 0), (257, 0), (384, 128), (513, 383)])
+def test_prefill_tile_boundaries(grout, S, P):
+    """Lengths and offsets around the 128-row / 256-row / 128-key tile edges."""
+    out, ref = _engine_case(grout, S, 16, 4, P, S + P + 7, seed=S + P)
+    _check(out, ref)
+
+
+def test_prefill_empty_is_a_no_op(grout):
+    q = torch.zeros(0, 8, D, dtype=torch.float16, device="cuda:0")
+    kc = torch.zeros(2, 16, D, dtype=torch.float16, device="cuda:0")
+    grout.attention_prefill(q, kc, kc.clone(), q.clone(), 0)
+    torch.cuda.synchronize()
+    grout.check_device_error()
