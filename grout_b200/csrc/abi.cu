@@ -135,6 +135,11 @@ int choose_splits(int32_t batch, int32_t max_kv_len, int32_t hkv, int num_sms) {
 
 void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
 
+int* device_error_word() {
+  DeviceState* ds;
+  return current_state(&ds) == GROUT_OK ? ds->err : nullptr;
+}
+
 }  // namespace grout
 
 using namespace grout;

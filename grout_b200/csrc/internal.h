@@ -11,6 +11,9 @@ constexpr int kHeadDim = 128;
 
 // Sets the message grout_attn_last_error() returns on this thread.
 void set_last_error(const char* msg);
+// Device error word of the current device (initialising it if needed), or
+// null if the device cannot be set up.
+int* device_error_word();
 
 struct NormRopeArgs {
   const __half* q;     // prefill: q rows; decode: qkv rows

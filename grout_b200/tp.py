@@ -1,0 +1,66 @@
+"""Tensor-parallel GEMV + all-reduce over NVLink peer memory (host side).
+
+TPComm wraps grout_tp_comm (include/grout_attn.h): it allocates this rank's
+receive/flag buffer, exchanges CUDA-IPC handles with the other ranks over a
+torch.distributed process group (host objects only), and opens the peers'
+buffers.  gemv_allreduce(w, x, residual, out) then computes, on every rank,
+out = residual + sum over ranks of w_r @ x_r in one kernel (partials stored
+directly into the peers' memory, per-block flags, bounded waits).  One
+process per GPU; all ranks must issue the same calls in the same order.
+"""
+import ctypes
+
+import torch
+
+from . import attn
+
+
+class TPComm:
+    def __init__(self, rank, world, hidden, group=None, device=None):
+        L = attn.lib()
+        self.rank, self.world, self.hidden = rank, world, hidden
+        dev = device or torch.device("cuda", torch.cuda.current_device())
+        nbytes = L.grout_tp_comm_bytes(world, hidden)
+        if nbytes == 0:
+            raise attn.GroutError(1, f"tp comm: unsupported world={world} hidden={hidden}")
+        self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        handle = (ctypes.c_char * 64)()
+        attn._check(L.grout_tp_ipc_handle(ctypes.c_void_p(self.buf.data_ptr()), handle))
+        mine = bytes(handle)
+        if world > 1:
+            allh = [None] * world
+            torch.distributed.all_gather_object(allh, mine, group=group)
+        else:
+            allh = [mine]
+        blob = (ctypes.c_char * (64 * world)).from_buffer_copy(b"".join(allh))
+        out = ctypes.c_void_p()
+        attn._check(L.grout_tp_comm_create(rank, world, hidden,
+                                           ctypes.c_void_p(self.buf.data_ptr()), blob,
+                                           ctypes.byref(out)))
+        self.comm = out
+        if world > 1:  # every rank has opened every buffer before anyone writes
+            torch.distributed.barrier(group=group)
+
+    def gemv_allreduce(self, w, x, out, residual=None):
+        """out[hidden] = residual + all-reduce(w @ x); w [hidden, k] f16
+        (this rank's shard), x [k] f16 (any leading dims of size 1)."""
+        L = attn.lib()
+        k = w.shape[1]
+        attn._need(w.shape[0] == self.hidden and x.numel() == k and out.numel() == self.hidden,
+                   "gemv_allreduce shape mismatch")
+        attn._check(L.grout_gemv_allreduce(
+            self.comm, ctypes.c_void_p(w.data_ptr()), k, ctypes.c_void_p(x.data_ptr()),
+            ctypes.c_void_p(residual.data_ptr()) if residual is not None else None,
+            ctypes.c_void_p(out.data_ptr()), attn._stream(x)))
+        return out
+
+    def close(self):
+        if self.comm:
+            attn.lib().grout_tp_comm_destroy(self.comm)
+            self.comm = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,149 @@
+"""GPU checks of the tensor-parallel GEMV + all-reduce (grout_gemv_allreduce).
+
+Numerics against a torch fp32 reference (the kernel accumulates in f32 and
+rounds the final sum to f16 once): max-abs <= 2e-3 relative to the output
+scale.  Multi-rank cases run one child process per GPU (skipped with fewer
+than two GPUs); the host side of the handle exchange uses gloo."""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+HIDDEN = 5120
+
+
+def _ref(ws, xs, residual):
+    y = sum(w.float() @ x.float() for w, x in zip(ws, xs))
+    return y + residual.float()
+
+
+def _inputs(rank, k, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed * 100 + rank)
+    w = (torch.randn(HIDDEN, k, device="cuda", generator=g) * 0.02).half()
+    x = torch.randn(k, device="cuda", generator=g).half()
+    return w, x
+
+
+def _tol(ref):
+    return 2e-3 * max(1.0, ref.abs().max().item())
+
+
+def test_gemv_allreduce_single_rank(grout):
+    from grout_b200 import tp
+    comm = tp.TPComm(0, 1, HIDDEN)
+    for k in (1024, 4096, 12800):
+        w, x = _inputs(0, k, seed=k)
+        res = torch.randn(HIDDEN, device="cuda").half()
+        out = torch.empty(HIDDEN, device="cuda", dtype=torch.float16)
+        for _ in range(3):  # successive calls alternate receive slots
+            comm.gemv_allreduce(w, x, out, residual=res)
+            torch.cuda.synchronize()
+            ref = _ref([w], [x], res)
+            assert (out.float() - ref).abs().max().item() <= _tol(ref)
+    # recorded once in a CUDA graph, replayed with new inputs
+    w, x = _inputs(0, 4096, seed=7)
+    out = torch.empty(HIDDEN, device="cuda", dtype=torch.float16)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        comm.gemv_allreduce(w, x, out)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        comm.gemv_allreduce(w, x, out)
+    for i in range(3):
+        x.copy_(torch.randn(4096, device="cuda").half())
+        g.replay()
+        torch.cuda.synchronize()
+        ref = _ref([w], [x], torch.zeros(HIDDEN, device="cuda"))
+        assert (out.float() - ref).abs().max().item() <= _tol(ref)
+    grout.check_device_error()
+    comm.close()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, k, mode, q):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import grout_b200 as g
+        from grout_b200 import tp
+        g.init(rank)
+        comm = tp.TPComm(rank, world, HIDDEN)
+        res = torch.full((HIDDEN,), 0.5, device="cuda").half()
+        out = torch.empty(HIDDEN, device="cuda", dtype=torch.float16)
+        if mode == "timeout":
+            # rank 1 leaves between steps: it never makes the call, so rank 0's
+            # bounded wait must expire and report a device error.
+            if rank == 0:
+                w, x = _inputs(rank, k)
+                comm.gemv_allreduce(w, x, out, residual=res)
+                torch.cuda.synchronize()
+                try:
+                    g.check_device_error()
+                    q.put((rank, "no-error"))
+                except g.GroutError as e:
+                    q.put((rank, "error:" + str(e)))
+            else:
+                q.put((rank, "skipped"))
+            dist.barrier()
+            return
+        outs = []
+        for step in range(4):
+            w, x = _inputs(rank, k, seed=step)
+            comm.gemv_allreduce(w, x, out, residual=res)
+            torch.cuda.synchronize()
+            allx = [_inputs(r, k, seed=step) for r in range(world)]
+            ref = _ref([a for a, _ in allx], [b for _, b in allx], res)
+            err = (out.float() - ref).abs().max().item()
+            outs.append((err, _tol(ref), out.cpu().view(torch.int16).clone()))
+        g.check_device_error()
+        comm.close()
+        q.put((rank, outs))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def _spawn(world, k, mode):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, k, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return res
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("k", [4096, 12800])
+def test_gemv_allreduce_two_ranks(k):
+    res = _spawn(2, k, "sum")
+    for step in range(4):
+        e0, t0, o0 = res[0][step]
+        e1, t1, o1 = res[1][step]
+        assert e0 <= t0 and e1 <= t1
+        assert torch.equal(o0, o1)  # identical bits on every rank
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_gemv_allreduce_missing_peer_times_out():
+    res = _spawn(2, 4096, "timeout")
+    assert res[1] == "skipped"
+    assert res[0].startswith("error:") and "0x13c" in res[0]
