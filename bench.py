@@ -350,7 +350,8 @@ def config5(args, rank, world, dist):
     c = qwen3_tp.Qwen3Shape()
     r = qwen3_tp.run_config5(rank, world, None, prompt_len=args.c5_prompt,
                              gen_tokens=args.c5_tokens, shape=c,
-                             barrier=dist.barrier if dist else None)
+                             barrier=dist.barrier if dist else None,
+                             fused_allreduce=not args.c5_nccl)
     dev = torch.device("cuda", torch.cuda.current_device())
     vals = reduce_max([r["decode_ms"], r["prefill_ms"], r["attn_ms_per_step"]], dist, dev)
     decode_ms, prefill_ms, attn_ms = vals
@@ -369,7 +370,8 @@ def config5(args, rank, world, dist):
             "attention_ms_per_token": round(attn_ms, 4),
             "attention_share": round(attn_ms / step_ms, 4),
             "roofline_tok_s": round(roof, 1), "frac": round(args.c5_tokens / (decode_ms * 1e-3) / roof, 4),
-            "bytes_per_token_per_rank": w_bytes + kv_bytes, "first_tokens": r["first_tokens"]}
+            "bytes_per_token_per_rank": w_bytes + kv_bytes, "first_tokens": r["first_tokens"],
+            "allreduce": r["allreduce"]}
 
 
 def ragged_c4(args, dev, rank, world, dist):
@@ -517,6 +519,8 @@ def main():
     ap.add_argument("--no-e2e-decode", action="store_true", help="skip config 5 (Qwen3-32B decode)")
     ap.add_argument("--c5-prompt", type=int, default=8192)
     ap.add_argument("--c5-tokens", type=int, default=256)
+    ap.add_argument("--c5-nccl", action="store_true",
+                    help="config 5 with cuBLAS GEMV + NCCL all-reduce instead of the fused kernel")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the prefill workload (decode grid only; for profiling)")
     ap.add_argument("--decode-cells", default="",

@@ -96,9 +96,8 @@ SIGNATURES = {
                                          _vp, _sz, _vp]),
     "grout_attn_decode_ex": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i32, _i32, _i32,
                                             _DIMS, _vp, _sz, _vp]),
-    "grout_tp_comm_bytes": (_sz, [_i32, _i32]),
-    "grout_tp_ipc_handle": (ctypes.c_int, [_vp, _vp]),
-    "grout_tp_comm_create": (ctypes.c_int, [_i32, _i32, _i32, _vp, _vp, ctypes.POINTER(_vp)]),
+    "grout_tp_comm_create": (ctypes.c_int, [_i32, _i32, ctypes.POINTER(_vp), _vp]),
+    "grout_tp_comm_connect": (ctypes.c_int, [_vp, _i32, _vp]),
     "grout_tp_comm_destroy": (None, [_vp]),
     "grout_gemv_allreduce": (ctypes.c_int, [_vp, _vp, _i32, _vp, _vp, _vp, _vp]),
     "grout_attn_decode_noalloc_max_bytes": (_sz, []),

@@ -38,7 +38,8 @@ constexpr int kThreads = 256;
 constexpr int kMaxK = 16384;      // x held in shared memory
 
 // Per-rank buffer layout (bytes): recv [2][world][hidden] f32 | flags
-// [world][kCtas] u32 | epoch [kCtas] u32.
+// [world][kCtas] u32 | epoch [kCtas] u32 | broken u32 (set once any wait of
+// this rank timed out: the ranks are out of step, later calls fail at once).
 __host__ __device__ inline size_t recv_bytes(int world, int hidden) {
   return (size_t)2 * world * hidden * 4;
 }
@@ -46,8 +47,11 @@ __host__ __device__ inline size_t flags_off(int world, int hidden) { return recv
 __host__ __device__ inline size_t epoch_off(int world, int hidden) {
   return flags_off(world, hidden) + (size_t)world * kCtas * 4;
 }
-__host__ __device__ inline size_t total_bytes(int world, int hidden) {
+__host__ __device__ inline size_t broken_off(int world, int hidden) {
   return epoch_off(world, hidden) + (size_t)kCtas * 4;
+}
+__host__ __device__ inline size_t total_bytes(int world, int hidden) {
+  return broken_off(world, hidden) + 16;
 }
 
 struct PeerPtrs {
@@ -77,7 +81,14 @@ __global__ void __launch_bounds__(kThreads) gemv_allreduce_kernel(
 
   unsigned char* mine = peers.base[rank];
   unsigned* epoch_p = reinterpret_cast<unsigned*>(mine + epoch_off(world, hidden)) + cta;
-  if (threadIdx.x == 0) s_epoch = *epoch_p;
+  volatile unsigned* broken = reinterpret_cast<unsigned*>(mine + broken_off(world, hidden));
+  if (threadIdx.x == 0) {
+    s_epoch = *epoch_p;
+    s_ok = *broken == 0u;
+    if (!s_ok && err) atomicCAS(err, 0, DEV_ERR_TIMEOUT_BASE + 61);
+  }
+  __syncthreads();
+  if (!s_ok) return;  // an earlier call lost step with the peers
   for (int i = threadIdx.x * 8; i < k; i += kThreads * 8)
     *reinterpret_cast<uint4*>(&xs[i]) = __ldg(reinterpret_cast<const uint4*>(x + i));
   __syncthreads();
@@ -131,6 +142,7 @@ __global__ void __launch_bounds__(kThreads) gemv_allreduce_kernel(
       while (ld_acquire_sys(f) != epoch) {
         if ((++spins & 255u) == 0 && globaltimer() - t0 > kWaitTimeoutNs) {
           s_ok = 0;
+          *broken = 1u;
           if (err) atomicCAS(err, 0, DEV_ERR_TIMEOUT_BASE + 60);
           break;
         }
@@ -154,88 +166,83 @@ __global__ void __launch_bounds__(kThreads) gemv_allreduce_kernel(
 }  // namespace grout
 
 struct grout_tp_comm {
-  int rank, world, hidden, device;
-  grout::PeerPtrs peers;
-  bool opened[grout::kMaxWorld];
-  int* err;
+  int rank = -1, world = 0, hidden = 0, device = 0;
+  grout::PeerPtrs peers{};
+  bool opened[grout::kMaxWorld] = {};
+  void* local = nullptr;  // this rank's exchange buffer (cudaMalloc, offset 0)
+  int* err = nullptr;
 };
 
 using namespace grout;
 
+namespace {
+grout_status tp_fail(grout_status st, const char* what, cudaError_t e) {
+  char m[200];
+  snprintf(m, sizeof(m), "%s: %s", what, e == cudaSuccess ? "" : cudaGetErrorString(e));
+  set_last_error(m);
+  return st;
+}
+}  // namespace
+
 extern "C" {
 
-size_t grout_tp_comm_bytes(int32_t world, int32_t hidden) {
-  if (world < 1 || world > kMaxWorld || hidden <= 0) return 0;
-  return total_bytes(world, hidden);
-}
-
-grout_status grout_tp_ipc_handle(void* local_buf, void* handle_out) {
-  if (!local_buf || !handle_out) {
-    set_last_error("null pointer argument");
-    return GROUT_ERR_INVALID_ARG;
-  }
-  cudaIpcMemHandle_t h;
-  cudaError_t e = cudaIpcGetMemHandle(&h, local_buf);
-  if (e != cudaSuccess) {
-    char m[160];
-    snprintf(m, sizeof(m), "cudaIpcGetMemHandle failed: %s", cudaGetErrorString(e));
-    set_last_error(m);
-    return GROUT_ERR_CUDA;
-  }
-  static_assert(sizeof(h) == GROUT_IPC_HANDLE_BYTES, "IPC handle size");
-  std::memcpy(handle_out, &h, sizeof(h));
-  return GROUT_OK;
-}
-
-grout_status grout_tp_comm_create(int32_t rank, int32_t world, int32_t hidden, void* local_buf,
-                                  const void* peer_handles, grout_tp_comm** out) {
-  if (!out || !local_buf || (world > 1 && !peer_handles)) {
-    set_last_error("null pointer argument");
-    return GROUT_ERR_INVALID_ARG;
-  }
-  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || hidden <= 0 ||
-      hidden % 8) {
-    set_last_error("tp comm: need 1 <= world <= 8, 0 <= rank < world, hidden % 8 == 0");
-    return GROUT_ERR_INVALID_ARG;
-  }
+grout_status grout_tp_comm_create(int32_t world, int32_t hidden, grout_tp_comm** comm,
+                                  void* handle_out) {
+  if (!comm || !handle_out) return tp_fail(GROUT_ERR_INVALID_ARG, "null pointer argument", cudaSuccess);
+  if (world < 1 || world > kMaxWorld || hidden <= 0 || hidden % 8)
+    return tp_fail(GROUT_ERR_INVALID_ARG, "tp comm: need 1 <= world <= 8 and hidden % 8 == 0",
+                   cudaSuccess);
   grout_tp_comm* c = new grout_tp_comm();
-  c->rank = rank;
   c->world = world;
   c->hidden = hidden;
   cudaGetDevice(&c->device);
-  for (int p = 0; p < world; ++p) {
+  // The buffer is the library's own allocation so that its IPC handle maps
+  // exactly this address in the peers (a sub-allocation of a caching
+  // allocator would map the enclosing block instead).
+  cudaError_t e = cudaMalloc(&c->local, total_bytes(world, hidden));
+  if (e == cudaSuccess) e = cudaMemset(c->local, 0, total_bytes(world, hidden));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, c->local);
+  if (e != cudaSuccess) {
+    if (c->local) cudaFree(c->local);
+    delete c;
+    return tp_fail(GROUT_ERR_CUDA, "tp comm setup", e);
+  }
+  static_assert(sizeof(h) == GROUT_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle_out, &h, sizeof(h));
+  c->err = device_error_word();
+  *comm = c;
+  return GROUT_OK;
+}
+
+grout_status grout_tp_comm_connect(grout_tp_comm* c, int32_t rank, const void* all_handles) {
+  if (!c || (c->world > 1 && !all_handles))
+    return tp_fail(GROUT_ERR_INVALID_ARG, "null pointer argument", cudaSuccess);
+  if (rank < 0 || rank >= c->world || c->rank >= 0)
+    return tp_fail(GROUT_ERR_INVALID_ARG, "tp comm: bad rank or already connected", cudaSuccess);
+  for (int p = 0; p < c->world; ++p) {
     if (p == rank) {
-      c->peers.base[p] = static_cast<unsigned char*>(local_buf);
+      c->peers.base[p] = static_cast<unsigned char*>(c->local);
       continue;
     }
     cudaIpcMemHandle_t h;
-    std::memcpy(&h, static_cast<const char*>(peer_handles) + (size_t)p * GROUT_IPC_HANDLE_BYTES,
+    std::memcpy(&h, static_cast<const char*>(all_handles) + (size_t)p * GROUT_IPC_HANDLE_BYTES,
                 sizeof(h));
     void* ptr = nullptr;
     cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
     if (e != cudaSuccess) {
-      char m[160];
-      snprintf(m, sizeof(m), "cudaIpcOpenMemHandle(rank %d) failed: %s", p,
-               cudaGetErrorString(e));
-      set_last_error(m);
       for (int q = 0; q < p; ++q)
-        if (c->opened[q]) cudaIpcCloseMemHandle(c->peers.base[q]);
-      delete c;
-      return GROUT_ERR_CUDA;
+        if (c->opened[q]) {
+          cudaIpcCloseMemHandle(c->peers.base[q]);
+          c->opened[q] = false;
+        }
+      return tp_fail(GROUT_ERR_CUDA, "cudaIpcOpenMemHandle", e);
     }
     c->peers.base[p] = static_cast<unsigned char*>(ptr);
     c->opened[p] = true;
   }
-  // This rank's flags and epochs start at zero (an init-time call).
-  cudaError_t e = cudaMemset(local_buf, 0, total_bytes(world, hidden));
-  if (e == cudaSuccess) e = cudaDeviceSynchronize();
-  if (e != cudaSuccess) {
-    set_last_error(cudaGetErrorString(e));
-    grout_tp_comm_destroy(c);
-    return GROUT_ERR_CUDA;
-  }
-  c->err = device_error_word();
-  *out = c;
+  c->rank = rank;
   return GROUT_OK;
 }
 
@@ -243,34 +250,28 @@ void grout_tp_comm_destroy(grout_tp_comm* c) {
   if (!c) return;
   for (int p = 0; p < c->world; ++p)
     if (c->opened[p]) cudaIpcCloseMemHandle(c->peers.base[p]);
+  if (c->local) cudaFree(c->local);
   delete c;
 }
 
 grout_status grout_gemv_allreduce(grout_tp_comm* c, const void* w, int32_t k, const void* x,
                                   const void* residual, void* out, grout_stream_t stream) {
-  if (!c || !w || !x || !out) {
-    set_last_error("null pointer argument");
-    return GROUT_ERR_INVALID_ARG;
-  }
-  if (k <= 0 || k % 8 || k > kMaxK) {
-    set_last_error("gemv_allreduce: k must be a positive multiple of 8, at most 16384");
-    return GROUT_ERR_INVALID_ARG;
-  }
+  if (!c || !w || !x || !out) return tp_fail(GROUT_ERR_INVALID_ARG, "null pointer argument", cudaSuccess);
+  if (c->rank < 0) return tp_fail(GROUT_ERR_INVALID_ARG, "tp comm not connected", cudaSuccess);
+  if (k <= 0 || k % 8 || k > kMaxK)
+    return tp_fail(GROUT_ERR_INVALID_ARG,
+                   "gemv_allreduce: k must be a positive multiple of 8, at most 16384", cudaSuccess);
   const void* ptrs[] = {w, x, out};
   for (const void* p : ptrs)
-    if (reinterpret_cast<uintptr_t>(p) & 15) {
-      set_last_error("gemv_allreduce: pointers must be 16-byte aligned");
-      return GROUT_ERR_INVALID_ARG;
-    }
+    if (reinterpret_cast<uintptr_t>(p) & 15)
+      return tp_fail(GROUT_ERR_INVALID_ARG, "gemv_allreduce: pointers must be 16-byte aligned",
+                     cudaSuccess);
   gemv_allreduce_kernel<<<kCtas, kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       c->peers, c->rank, c->world, c->hidden, k, static_cast<const __half*>(w),
       static_cast<const __half*>(x), static_cast<const __half*>(residual),
       static_cast<__half*>(out), c->err);
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    set_last_error(cudaGetErrorString(e));
-    return GROUT_ERR_CUDA;
-  }
+  if (e != cudaSuccess) return tp_fail(GROUT_ERR_CUDA, "gemv_allreduce launch", e);
   return GROUT_OK;
 }
 

@@ -47,7 +47,8 @@ def _rms(x, w, eps):
 
 
 class Qwen3TP:
-    def __init__(self, shape, max_seq, rank=0, world=1, group=None, device=None, seed=6):
+    def __init__(self, shape, max_seq, rank=0, world=1, group=None, device=None, seed=6,
+                 fused_allreduce=True):
         self.c = c = shape
         self.rank, self.world, self.group = rank, world, group
         self.dev = device or torch.device("cuda", torch.cuda.current_device())
@@ -86,6 +87,13 @@ class Qwen3TP:
         self.tok = torch.zeros(1, dtype=torch.int64, device=self.dev)
         nks = attn.decode_workspace_bytes(1, max_seq, self.hq, self.hkv, max_seq)
         self.ws = torch.empty(max(16, nks), dtype=torch.uint8, device=self.dev)
+        # Decode o_proj / down_proj: one grout kernel does the row-parallel GEMV,
+        # the all-reduce over NVLink and the residual add (TP > 1); otherwise
+        # cuBLAS + NCCL.
+        self.comm = None
+        if fused_allreduce and world > 1 and max(self.hq * D, self.it) <= 16384:
+            from .tp import TPComm
+            self.comm = TPComm(rank, world, H, group, self.dev)
         # decode-step buffers (fixed addresses for graph replay)
         self.q1 = torch.empty(1, self.hq, D, device=self.dev, dtype=torch.float16)
         self.o1 = torch.empty_like(self.q1)
@@ -150,11 +158,21 @@ class Qwen3TP:
                                   self.max_seq, workspace=self.ws)
             if attention_only:
                 continue
-            x = x + self._allreduce(F.linear(self.o1.view(1, -1), L["w_o"]))
+            if self.comm is not None:
+                x1 = torch.empty_like(x)
+                self.comm.gemv_allreduce(L["w_o"], self.o1, x1, residual=x)
+                x = x1
+            else:
+                x = x + self._allreduce(F.linear(self.o1.view(1, -1), L["w_o"]))
             h = _rms(x, L["post_norm"], c.eps)
             gu = F.linear(h, L["w_gu"])
-            a = F.silu(gu[:, : self.it]) * gu[:, self.it:]
-            x = x + self._allreduce(F.linear(a, L["w_down"]))
+            a = (F.silu(gu[:, : self.it]) * gu[:, self.it:]).contiguous()
+            if self.comm is not None:
+                x2 = torch.empty_like(x)
+                self.comm.gemv_allreduce(L["w_down"], a, x2, residual=x)
+                x = x2
+            else:
+                x = x + self._allreduce(F.linear(a, L["w_down"]))
         return x
 
     def _decode_step(self):
@@ -201,13 +219,13 @@ class Qwen3TP:
 
 
 def run_config5(rank=0, world=1, group=None, prompt_len=8192, gen_tokens=256, shape=None,
-                barrier=None):
+                barrier=None, fused_allreduce=True):
     """Config 5 measurement on this rank: returns a dict (rank 0 meaningful)."""
     c = shape or Qwen3Shape()
     dev = torch.device("cuda", torch.cuda.current_device())
     max_seq = prompt_len + gen_tokens
     t0 = time.perf_counter()
-    m = Qwen3TP(c, max_seq, rank, world, group, dev)
+    m = Qwen3TP(c, max_seq, rank, world, group, dev, fused_allreduce=fused_allreduce)
     torch.cuda.synchronize()
     t_init = time.perf_counter() - t0
     g = torch.Generator(device=dev).manual_seed(6)
@@ -251,4 +269,6 @@ def run_config5(rank=0, world=1, group=None, prompt_len=8192, gen_tokens=256, sh
     attn.check_device_error()
     return {"prefill_ms": prefill_ms, "decode_ms": decode_ms, "gen_tokens": gen_tokens,
             "tok_s": gen_tokens / (decode_ms * 1e-3), "step_ms": decode_ms / gen_tokens,
-            "attn_ms_per_step": attn_ms, "init_s": t_init, "first_tokens": toks[:4]}
+            "attn_ms_per_step": attn_ms, "init_s": t_init, "first_tokens": toks[:4],
+            "allreduce": "grout fused GEMV+all-reduce (NVLink P2P)" if m.comm is not None
+                         else ("none" if world == 1 else "NCCL")}

@@ -1,9 +1,9 @@
 """Tensor-parallel GEMV + all-reduce over NVLink peer memory (host side).
 
-TPComm wraps grout_tp_comm (include/grout_attn.h): it allocates this rank's
-receive/flag buffer, exchanges CUDA-IPC handles with the other ranks over a
-torch.distributed process group (host objects only), and opens the peers'
-buffers.  gemv_allreduce(w, x, residual, out) then computes, on every rank,
+TPComm wraps grout_tp_comm (include/grout_attn.h): the library allocates
+this rank's receive/flag buffer (its own cudaMalloc, so the IPC handle maps
+exactly that address), the handles are exchanged over a torch.distributed
+process group (host objects only), and the peers' buffers are opened.  gemv_allreduce(w, x, residual, out) then computes, on every rank,
 out = residual + sum over ranks of w_r @ x_r in one kernel (partials stored
 directly into the peers' memory, per-block flags, bounded waits).  One
 process per GPU; all ranks must issue the same calls in the same order.
@@ -19,13 +19,11 @@ class TPComm:
     def __init__(self, rank, world, hidden, group=None, device=None):
         L = attn.lib()
         self.rank, self.world, self.hidden = rank, world, hidden
-        dev = device or torch.device("cuda", torch.cuda.current_device())
-        nbytes = L.grout_tp_comm_bytes(world, hidden)
-        if nbytes == 0:
-            raise attn.GroutError(1, f"tp comm: unsupported world={world} hidden={hidden}")
-        self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        self.comm = None
         handle = (ctypes.c_char * 64)()
-        attn._check(L.grout_tp_ipc_handle(ctypes.c_void_p(self.buf.data_ptr()), handle))
+        out = ctypes.c_void_p()
+        attn._check(L.grout_tp_comm_create(world, hidden, ctypes.byref(out), handle))
+        self.comm = out
         mine = bytes(handle)
         if world > 1:
             allh = [None] * world
@@ -33,11 +31,7 @@ class TPComm:
         else:
             allh = [mine]
         blob = (ctypes.c_char * (64 * world)).from_buffer_copy(b"".join(allh))
-        out = ctypes.c_void_p()
-        attn._check(L.grout_tp_comm_create(rank, world, hidden,
-                                           ctypes.c_void_p(self.buf.data_ptr()), blob,
-                                           ctypes.byref(out)))
-        self.comm = out
+        attn._check(L.grout_tp_comm_connect(self.comm, rank, blob))
         if world > 1:  # every rank has opened every buffer before anyone writes
             torch.distributed.barrier(group=group)
 

@@ -217,27 +217,30 @@ grout_status grout_attn_decode_ex(const void* q, const void* k_cache, const void
 /* No counterpart in the reference (single-GPU); this is the row-parallel
  * o_proj / down_proj of a tensor-parallel decode step plus its all-reduce,
  * the next component after the attention path (config 5's layout).
- * Setup, once per rank (init-time; host exchange of IPC handles is the
- * caller's, e.g. an all-gather over torch.distributed):
- *   1. allocate grout_tp_comm_bytes(world, hidden) bytes of device memory;
- *   2. grout_tp_ipc_handle(buf, handle) -> GROUT_IPC_HANDLE_BYTES bytes;
- *   3. gather all ranks' handles into [world][GROUT_IPC_HANDLE_BYTES];
- *   4. grout_tp_comm_create(rank, world, hidden, buf, handles, &comm)
- *      (opens the peers' buffers, zeroes this rank's flags; synchronises).
+ * Setup, once per rank (init-time; the exchange of IPC handles between the
+ * processes is the caller's, e.g. an all-gather over torch.distributed):
+ *   1. grout_tp_comm_create(world, hidden, &comm, handle): allocates and
+ *      zeroes this rank's exchange buffer (cudaMalloc; 2*world*hidden*4 bytes
+ *      plus flags) and returns its GROUT_IPC_HANDLE_BYTES-byte IPC handle;
+ *   2. gather every rank's handle into [world][GROUT_IPC_HANDLE_BYTES];
+ *   3. grout_tp_comm_connect(comm, rank, handles) opens the peers' buffers;
+ *      all ranks must have connected before any rank calls
+ *      grout_gemv_allreduce (e.g. a barrier).
  * Per call, on every rank in the same order:
  *   out[hidden] = residual[hidden] (may be NULL) + sum over ranks of W_r x_r,
  *   W_r [hidden][k] f16 row-major (this rank's column shard), x_r [k] f16,
  *   k a multiple of 8, <= 16384.  Peers exchange f32 partials by direct
  *   stores over NVLink and per-block flags; every wait is bounded (2 s,
- *   then device error 0x13c and the output is left unwritten).  The result
- *   is bitwise identical on every rank.  Stream-ordered; a call recorded in a
- *   CUDA graph may be replayed (the sequence number lives on the device). */
+ *   then device error 0x13c, the output is left unwritten and the comm is
+ *   marked out of step: later calls return at once with device error
+ *   0x13d).  The result is bitwise identical on every rank.  Stream-ordered;
+ *   a call recorded in a CUDA graph may be replayed (the sequence number
+ *   lives on the device). */
 #define GROUT_IPC_HANDLE_BYTES 64
 typedef struct grout_tp_comm grout_tp_comm;
-size_t grout_tp_comm_bytes(int32_t world, int32_t hidden);
-grout_status grout_tp_ipc_handle(void* local_buf, void* handle_out);
-grout_status grout_tp_comm_create(int32_t rank, int32_t world, int32_t hidden, void* local_buf,
-                                  const void* peer_handles, grout_tp_comm** comm);
+grout_status grout_tp_comm_create(int32_t world, int32_t hidden, grout_tp_comm** comm,
+                                  void* handle_out);
+grout_status grout_tp_comm_connect(grout_tp_comm* comm, int32_t rank, const void* all_handles);
 void grout_tp_comm_destroy(grout_tp_comm* comm);
 grout_status grout_gemv_allreduce(grout_tp_comm* comm, const void* w, int32_t k, const void* x,
                                   const void* residual, void* out, grout_stream_t stream);

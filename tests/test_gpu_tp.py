@@ -80,6 +80,9 @@ def _worker(rank, world, port, k, mode, q):
         import grout_b200 as g
         from grout_b200 import tp
         g.init(rank)
+        # allocations before the comm, as in an engine: the exchange buffer
+        # must still be mapped at exactly its own address in the peer
+        junk = [torch.empty(12345 + 777 * i, device="cuda") for i in range(5)]
         comm = tp.TPComm(rank, world, HIDDEN)
         res = torch.full((HIDDEN,), 0.5, device="cuda").half()
         out = torch.empty(HIDDEN, device="cuda", dtype=torch.float16)
@@ -90,11 +93,24 @@ def _worker(rank, world, port, k, mode, q):
                 w, x = _inputs(rank, k)
                 comm.gemv_allreduce(w, x, out, residual=res)
                 torch.cuda.synchronize()
+                msgs = []
                 try:
                     g.check_device_error()
-                    q.put((rank, "no-error"))
+                    msgs.append("no-error")
                 except g.GroutError as e:
-                    q.put((rank, "error:" + str(e)))
+                    msgs.append("error:" + str(e))
+                # the comm is now out of step: the next call fails at once
+                import time
+                t0 = time.time()
+                comm.gemv_allreduce(w, x, out, residual=res)
+                torch.cuda.synchronize()
+                dt = time.time() - t0
+                try:
+                    g.check_device_error()
+                    msgs.append("no-error")
+                except g.GroutError as e:
+                    msgs.append("error:" + str(e))
+                q.put((rank, (msgs, dt)))
             else:
                 q.put((rank, "skipped"))
             dist.barrier()
@@ -146,4 +162,6 @@ def test_gemv_allreduce_two_ranks(k):
 def test_gemv_allreduce_missing_peer_times_out():
     res = _spawn(2, 4096, "timeout")
     assert res[1] == "skipped"
-    assert res[0].startswith("error:") and "0x13c" in res[0]
+    (first, second), dt = res[0]
+    assert first.startswith("error:") and "0x13c" in first
+    assert second.startswith("error:") and "0x13d" in second and dt < 1.0
