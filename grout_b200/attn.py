@@ -100,6 +100,7 @@ SIGNATURES = {
     "grout_tp_comm_connect": (ctypes.c_int, [_vp, _i32, _vp]),
     "grout_tp_comm_destroy": (None, [_vp]),
     "grout_gemv_allreduce": (ctypes.c_int, [_vp, _vp, _i32, _vp, _vp, _vp, _vp]),
+    "grout_allreduce_residual": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp]),
     "grout_attn_decode_noalloc_max_bytes": (_sz, []),
     "grout_attn_decode_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i32, _i32,
                                                  _DIMS, _vp]),

@@ -5,11 +5,12 @@
 // would need (it is single-GPU; the split is the Megatron layout of config 5).
 // One kernel per call on every rank:
 //   1. CTA i computes rows [i*R, (i+1)*R) of its partial W_r x_r in f32
-//      (one warp per row, 16-byte coalesced weight loads, x in shared memory);
+//      (each warp a K slice of eight rows at a time, 16-byte weight loads
+//      software-pipelined one step ahead, x in shared memory);
 //   2. it stores that slice into slot [epoch & 1][rank] of every peer's
 //      receive buffer (plain stores through the CUDA-IPC mapping over NVLink;
-//      no TMA, no multicast), fences at system scope and raises flag
-//      [rank][i] = epoch + 1 in every peer;
+//      no TMA, no multicast) and, after a CTA barrier, raises flag
+//      [rank][i] = epoch + 1 in every peer with a system-scope release store;
 //   3. it waits — bounded by a 2 s limit, after which it records a device
 //      error and writes nothing — for flag [p][i] == epoch + 1 from every
 //      peer p, then sums the partials in rank order 0..world-1 (identical
@@ -33,8 +34,10 @@ namespace grout {
 namespace {
 
 constexpr int kMaxWorld = 8;
-constexpr int kCtas = 128;        // CTAs per call (all resident: one per SM at most)
-constexpr int kThreads = 256;
+constexpr int kCtas = 148;        // CTAs per call (one per SM on B200)
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxRowsPerCta = 56;  // hidden <= 148 * 56
 constexpr int kMaxK = 16384;      // x held in shared memory
 
 // Per-rank buffer layout (bytes): recv [2][world][hidden] f32 | flags
@@ -77,7 +80,7 @@ __global__ void __launch_bounds__(kThreads) gemv_allreduce_kernel(
   const int cta = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rows = (hidden + kCtas - 1) / kCtas;
-  const int r0 = cta * rows, r1 = min(hidden, r0 + rows);
+  const int r0 = min(hidden, cta * rows), r1 = min(hidden, r0 + rows);
 
   unsigned char* mine = peers.base[rank];
   unsigned* epoch_p = reinterpret_cast<unsigned*>(mine + epoch_off(world, hidden)) + cta;
@@ -89,43 +92,100 @@ __global__ void __launch_bounds__(kThreads) gemv_allreduce_kernel(
   }
   __syncthreads();
   if (!s_ok) return;  // an earlier call lost step with the peers
-  for (int i = threadIdx.x * 8; i < k; i += kThreads * 8)
-    *reinterpret_cast<uint4*>(&xs[i]) = __ldg(reinterpret_cast<const uint4*>(x + i));
+  if (w)
+    for (int i = threadIdx.x * 8; i < k; i += blockDim.x * 8)
+      *reinterpret_cast<uint4*>(&xs[i]) = __ldg(reinterpret_cast<const uint4*>(x + i));
   __syncthreads();
   const unsigned epoch = s_epoch + 1;
   const int slot = epoch & 1;
 
-  // 1-2. partial rows, stored into every rank's receive slot [slot][rank]
-  for (int r = r0 + warp; r < r1; r += kThreads / 32) {
-    const __half* wr = w + (int64_t)r * k;
-    float acc = 0.f;
-    for (int c = lane * 8; c < k; c += 32 * 8) {
-      const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wr + c));
+  // 1. partial rows.  Warp w covers the K slice [k0, k1) of every row of
+  //    this CTA, eight rows per group; each lane holds one 16-byte chunk of
+  //    the eight rows, and the loads of the next (group, chunk) are issued
+  //    before the current one is consumed, so round trips overlap.  Warp
+  //    partials meet in shared memory and are summed in a fixed order.
+  __shared__ float red[kWarps][kMaxRowsPerCta];
+  const int nwarps = blockDim.x >> 5;
+  const int kw = ((k + nwarps - 1) / nwarps + 255) / 256 * 256;
+  const int k0 = warp * kw, k1 = min(k, k0 + kw);
+  const int nrows = r1 - r0;
+  const int ngroups = (nrows + 7) / 8;
+  const int nchunks = w ? max(0, (k1 - k0 + 255) / 256) : 0;
+  const int total = ngroups * nchunks;
+  auto load = [&](int it, uint4 (&wv)[8]) {
+    const int g = it / nchunks, ch = it - g * nchunks;
+    const int c = k0 + ch * 256 + lane * 8;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int r = r0 + g * 8 + u;
+      if (c < k1 && r < r1) wv[u] = __ldg(reinterpret_cast<const uint4*>(w + (int64_t)r * k + c));
+      else wv[u] = make_uint4(0, 0, 0, 0);
+    }
+  };
+  uint4 cur[8], nxt[8];
+  float acc[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) acc[u] = 0.f;
+  if (total > 0) load(0, cur);
+  for (int it = 0; it < total; ++it) {
+    if (it + 1 < total) load(it + 1, nxt);
+    const int g = it / nchunks, ch = it - g * nchunks;
+    const int c = k0 + ch * 256 + lane * 8;
+    if (c < k1) {
       const uint4 xv = *reinterpret_cast<const uint4*>(&xs[c]);
-      const __half2* wh = reinterpret_cast<const __half2*>(&wv);
       const __half2* xh = reinterpret_cast<const __half2*>(&xv);
+      float xf[8];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float2 a = __half22float2(wh[e]);
         const float2 b = __half22float2(xh[e]);
-        acc = fmaf(a.x, b.x, acc);
-        acc = fmaf(a.y, b.y, acc);
+        xf[2 * e] = b.x;
+        xf[2 * e + 1] = b.y;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const __half2* wh = reinterpret_cast<const __half2*>(&cur[u]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 a = __half22float2(wh[e]);
+          acc[u] = fmaf(a.x, xf[2 * e], acc[u]);
+          acc[u] = fmaf(a.y, xf[2 * e + 1], acc[u]);
+        }
+      }
+    }
+    if (ch == nchunks - 1) {  // group done: warp-reduce its eight rows
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        float v = acc[u];
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0 && g * 8 + u < nrows) red[warp][g * 8 + u] = v;
+        acc[u] = 0.f;
       }
     }
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (lane == 0) {
-      for (int p = 0; p < world; ++p) {
-        float* recv = reinterpret_cast<float*>(peers.base[p]) + ((size_t)slot * world + rank) * hidden;
-        recv[r] = acc;
-      }
+    for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
+  }
+  if (nchunks == 0 && lane == 0)  // this warp's K slice is empty
+    for (int i = 0; i < nrows; ++i) red[warp][i] = 0.f;
+  if (!w && warp == 0)  // exchange only: the partial is given (x[hidden])
+    for (int i = lane; i < nrows; i += 32) red[0][i] = __half2float(x[r0 + i]);
+  __syncthreads();
+  // The CTA's slice of partials goes into slot [slot][rank] of every rank's
+  // receive buffer.
+  if (threadIdx.x < nrows) {
+    float v = 0.f;
+    for (int ww = 0; ww < nwarps; ++ww) v += red[ww][threadIdx.x];
+    for (int p = 0; p < world; ++p) {
+      float* recv = reinterpret_cast<float*>(peers.base[p]) + ((size_t)slot * world + rank) * hidden;
+      recv[r0 + threadIdx.x] = v;
     }
   }
-  if (lane == 0) __threadfence_system();  // this warp's remote stores before the flags
+  // The CTA barrier orders every thread's partial stores before the flag
+  // stores below; st.release.sys makes them visible to a peer that reads the
+  // flag with ld.acquire.sys (release is cumulative over the barrier).
   __syncthreads();
-  // 2. flags: after a system-scope fence every peer may read our slice
+  // 2. flags: every peer may now read our slice
   if (threadIdx.x < world) {
-    __threadfence_system();
     const int p = threadIdx.x;
     unsigned* flag = reinterpret_cast<unsigned*>(peers.base[p] + flags_off(world, hidden)) +
                      rank * kCtas + cta;
@@ -154,7 +214,7 @@ __global__ void __launch_bounds__(kThreads) gemv_allreduce_kernel(
   __syncthreads();
   if (!s_ok) return;
   const float* recv = reinterpret_cast<const float*>(mine) + (size_t)slot * world * hidden;
-  for (int r = r0 + threadIdx.x; r < r1; r += kThreads) {
+  for (int r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
     float y = 0.f;
     for (int p = 0; p < world; ++p) y += __ldcg(recv + (size_t)p * hidden + r);
     if (residual) y += __half2float(residual[r]);
@@ -189,9 +249,10 @@ extern "C" {
 grout_status grout_tp_comm_create(int32_t world, int32_t hidden, grout_tp_comm** comm,
                                   void* handle_out) {
   if (!comm || !handle_out) return tp_fail(GROUT_ERR_INVALID_ARG, "null pointer argument", cudaSuccess);
-  if (world < 1 || world > kMaxWorld || hidden <= 0 || hidden % 8)
-    return tp_fail(GROUT_ERR_INVALID_ARG, "tp comm: need 1 <= world <= 8 and hidden % 8 == 0",
-                   cudaSuccess);
+  if (world < 1 || world > kMaxWorld || hidden <= 0 || hidden % 8 ||
+      hidden > kCtas * kMaxRowsPerCta)
+    return tp_fail(GROUT_ERR_INVALID_ARG,
+                   "tp comm: need 1 <= world <= 8, hidden % 8 == 0, hidden <= 8288", cudaSuccess);
   grout_tp_comm* c = new grout_tp_comm();
   c->world = world;
   c->hidden = hidden;
@@ -272,6 +333,19 @@ grout_status grout_gemv_allreduce(grout_tp_comm* c, const void* w, int32_t k, co
       static_cast<__half*>(out), c->err);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return tp_fail(GROUT_ERR_CUDA, "gemv_allreduce launch", e);
+  return GROUT_OK;
+}
+
+grout_status grout_allreduce_residual(grout_tp_comm* c, const void* partial, const void* residual,
+                                      void* out, grout_stream_t stream) {
+  if (!c || !partial || !out)
+    return tp_fail(GROUT_ERR_INVALID_ARG, "null pointer argument", cudaSuccess);
+  if (c->rank < 0) return tp_fail(GROUT_ERR_INVALID_ARG, "tp comm not connected", cudaSuccess);
+  gemv_allreduce_kernel<<<kCtas, 64, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      c->peers, c->rank, c->world, c->hidden, 0, nullptr, static_cast<const __half*>(partial),
+      static_cast<const __half*>(residual), static_cast<__half*>(out), c->err);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return tp_fail(GROUT_ERR_CUDA, "allreduce launch", e);
   return GROUT_OK;
 }
 

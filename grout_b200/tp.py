@@ -48,6 +48,17 @@ class TPComm:
             ctypes.c_void_p(out.data_ptr()), attn._stream(x)))
         return out
 
+    def allreduce(self, partial, out, residual=None):
+        """out[hidden] = residual + all-reduce(partial); partial [hidden] f16."""
+        L = attn.lib()
+        attn._need(partial.numel() == self.hidden and out.numel() == self.hidden,
+                   "allreduce shape mismatch")
+        attn._check(L.grout_allreduce_residual(
+            self.comm, ctypes.c_void_p(partial.data_ptr()),
+            ctypes.c_void_p(residual.data_ptr()) if residual is not None else None,
+            ctypes.c_void_p(out.data_ptr()), attn._stream(partial)))
+        return out
+
     def close(self):
         if self.comm:
             attn.lib().grout_tp_comm_destroy(self.comm)

@@ -229,7 +229,7 @@ grout_status grout_attn_decode_ex(const void* q, const void* k_cache, const void
  * Per call, on every rank in the same order:
  *   out[hidden] = residual[hidden] (may be NULL) + sum over ranks of W_r x_r,
  *   W_r [hidden][k] f16 row-major (this rank's column shard), x_r [k] f16,
- *   k a multiple of 8, <= 16384.  Peers exchange f32 partials by direct
+ *   k a multiple of 8, <= 16384, hidden <= 8288.  Peers exchange f32 partials by direct
  *   stores over NVLink and per-block flags; every wait is bounded (2 s,
  *   then device error 0x13c, the output is left unwritten and the comm is
  *   marked out of step: later calls return at once with device error
@@ -244,6 +244,12 @@ grout_status grout_tp_comm_connect(grout_tp_comm* comm, int32_t rank, const void
 void grout_tp_comm_destroy(grout_tp_comm* comm);
 grout_status grout_gemv_allreduce(grout_tp_comm* comm, const void* w, int32_t k, const void* x,
                                   const void* residual, void* out, grout_stream_t stream);
+/* The same exchange without the GEMV: out = residual (may be NULL) + sum over
+ * ranks of partial_r, partial_r [hidden] f16 computed by the caller (e.g. a
+ * cuBLAS GEMV).  Same ordering, bounds and errors as grout_gemv_allreduce;
+ * the two may be interleaved on one comm. */
+grout_status grout_allreduce_residual(grout_tp_comm* comm, const void* partial,
+                                      const void* residual, void* out, grout_stream_t stream);
 
 /* Allocation-free decode.  No counterpart in the reference.  For callers that
  * cannot provide a device workspace — an engine whose device memory is all

@@ -118,7 +118,10 @@ def _worker(rank, world, port, k, mode, q):
         outs = []
         for step in range(4):
             w, x = _inputs(rank, k, seed=step)
-            comm.gemv_allreduce(w, x, out, residual=res)
+            if step % 2:  # alternate with the exchange-only entry on the same comm
+                comm.allreduce((w.float() @ x.float()).half(), out, residual=res)
+            else:
+                comm.gemv_allreduce(w, x, out, residual=res)
             torch.cuda.synchronize()
             allx = [_inputs(r, k, seed=step) for r in range(world)]
             ref = _ref([a for a, _ in allx], [b for _, b in allx], res)
@@ -154,7 +157,8 @@ def test_gemv_allreduce_two_ranks(k):
     for step in range(4):
         e0, t0, o0 = res[0][step]
         e1, t1, o1 = res[1][step]
-        assert e0 <= t0 and e1 <= t1
+        tol = 2 * t0 if step % 2 else t0  # exchange-only sums f16-rounded partials
+        assert e0 <= tol and e1 <= tol
         assert torch.equal(o0, o1)  # identical bits on every rank
 
 
