@@ -10,8 +10,12 @@
 //   warps 0-3  softmax for query tile 0 (one thread per query row = TMEM lane)
 //   warps 4-7  softmax for query tile 1
 //   warp 8     TMA producer: Q tiles once, then K_j, V_j into a 4-slot ring
-//   warp 9     MMA issuer (one thread): tcgen05.mma, completion via
-//              tcgen05.commit on mbarriers
+//   warp 9     MMA issuer: the whole warp runs the issue loop (so its
+//              descriptors stay warp-uniform) and one elected lane issues
+//              every tcgen05.mma and tcgen05.commit.  This warp shares its
+//              SM sub-partition with two busy softmax warps, so each MMA is
+//              kept to a few instructions: descriptors are precomputed low
+//              words advanced by constant adds.
 //   warps 10-11 idle (they complete the third warpgroup, whose registers
 //              setmaxnreg hands to the softmax warpgroups)
 // Tensor memory (512 columns, f32): S0 [0,128) S1 [128,256) O0 [256,384)
@@ -121,6 +125,33 @@ constexpr float kRescaleThreshold = 8.0f;
 __device__ __forceinline__ int ring_slot(int i) { return i % kSlots; }
 __device__ __forceinline__ uint32_t ring_parity(int i) { return (uint32_t)((i / kSlots) & 1); }
 
+// Low/high words of the SW128 shared-memory descriptor (matches
+// smem_desc_sw128): low = start address >> 4 | LBO >> 4 << 16;
+// high = SBO (1024) >> 4 | version 1 << 14 | layout SW128 (2) << 29.
+constexpr uint32_t kDescLboK = (16u >> 4) << 16;
+constexpr uint32_t kDescLboV = ((uint32_t)kBox >> 4) << 16;
+constexpr uint32_t kDescHi = (1024u >> 4) | (1u << 14) | (2u << 29);
+static_assert(((uint64_t)kDescHi << 32) == ((uint64_t)(1024u >> 4) << 32 | 1ull << 46 | 2ull << 61),
+              "descriptor high word");
+__device__ __forceinline__ void mma_ss_lo(uint32_t d, uint32_t alo, uint32_t blo, uint32_t idesc,
+                                          uint32_t acc) {
+  asm volatile(
+      "{ .reg .pred p; .reg .b64 da, db; setp.ne.u32 p, %4, 0;"
+      " mov.b64 da, {%1, %5}; mov.b64 db, {%2, %5};"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p; }" ::"r"(d),
+      "r"(alo), "r"(blo), "r"(idesc), "r"(acc), "n"(kDescHi)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_lo(uint32_t d, uint32_t a_tmem, uint32_t blo, uint32_t idesc,
+                                          uint32_t acc) {
+  asm volatile(
+      "{ .reg .pred p; .reg .b64 db; setp.ne.u32 p, %4, 0;"
+      " mov.b64 db, {%2, %5};"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %3, p; }" ::"r"(d),
+      "r"(a_tmem), "r"(blo), "r"(idesc), "r"(acc), "n"(kDescHi)
+      : "memory");
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
@@ -215,25 +246,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------- MMA issue
-    if (lane == 0) {
+    // The whole warp runs the issue loop (warp-uniform descriptors); one
+    // elected lane issues every MMA and commit.
+    {
+      const bool leader = elect_one();
       constexpr uint32_t idesc_qk = idesc_f16_f32(kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = idesc_f16_f32(kBM, 128, 0, 1);
+      // Shared-memory descriptors as (low word, constant high word): the
+      // start-address field of the low word is advanced by plain adds (all
+      // addresses are below 256 KB, so the 14-bit field never carries).
+      const uint32_t base16 = smem_base >> 4;
       auto qk = [&](int t, int slot) {
-        const uint32_t qa = smem_base + kOffQ + t * kTile;
-        const uint32_t kb = smem_base + kOffKV + slot * kTile;
+        const uint32_t qlo = base16 + (kOffQ + t * kTile) / 16 + kDescLboK;
+        const uint32_t klo = base16 + (kOffKV + slot * kTile) / 16 + kDescLboK;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
-          tc_mma_ss(tmem + t * 128, smem_desc_sw128(qa + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024),
-                    idesc_qk, kk > 0 ? 1u : 0u);
+          const uint32_t off = ((kk >> 2) * kBox + (kk & 3) * 32) / 16;
+          if (leader) mma_ss_lo(tmem + t * 128, qlo + off, klo + off, idesc_qk, kk > 0 ? 1u : 0u);
         }
       };
       auto pv = [&](int t, int slot, bool acc) {
-        const uint32_t vb = smem_base + kOffKV + slot * kTile;
+        const uint32_t vlo = base16 + (kOffKV + slot * kTile) / 16 + kDescLboV;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          tc_mma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, smem_desc_sw128(vb + kk * 2048, kBox, 1024), idesc_pv,
-                    (acc || kk > 0) ? 1u : 0u);
+          if (leader) mma_ts_lo(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, vlo + kk * (2048 / 16), idesc_pv,
+                                (acc || kk > 0) ? 1u : 0u);
         }
       };
       bool ok = mbar_wait(smem_u32(&bars[kBarQ]), 0, a.err, 20, abort_flag);
@@ -242,16 +279,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) {
         tc_fence_after();
         qk(0, ring_slot(0));
-        tc_commit(smem_u32(&bars[kBarS + 0]));
+        if (leader) tc_commit(smem_u32(&bars[kBarS + 0]));
         qk(1, ring_slot(0));
-        tc_commit(smem_u32(&bars[kBarS + 1]));
-        tc_commit(smem_u32(&bars[kBarEmpty + ring_slot(0)]));
+        if (leader) tc_commit(smem_u32(&bars[kBarS + 1]));
+        if (leader) tc_commit(smem_u32(&bars[kBarEmpty + ring_slot(0)]));
         for (int j = 0; j < n_kv && ok; ++j) {
           const int iv = 2 * j + 1, ik = 2 * j + 2;
           const bool next = j + 1 < n_kv;
           ok = mbar_wait(smem_u32(&bars[kBarFull + ring_slot(iv)]), ring_parity(iv), a.err, 22,
                          abort_flag);
           if (!ok) break;
+          // K(j+1) only needs the slot K(j-1) released, so it is awaited
+          // here, before P0(j), keeping the wait off the PV0 -> QK0 path.
+          if (next) {
+            ok = mbar_wait(smem_u32(&bars[kBarFull + ring_slot(ik)]), ring_parity(ik), a.err, 24,
+                           abort_flag);
+            if (!ok) break;
+          }
           if (j < n_kv0) {
             ok = mbar_wait(smem_u32(&bars[kBarP + 0]), j & 1, a.err, 23, abort_flag);
             if (!ok) break;
@@ -259,27 +303,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             pv(0, ring_slot(iv), j > 0);
           }
           if (next) {
-            ok = mbar_wait(smem_u32(&bars[kBarFull + ring_slot(ik)]), ring_parity(ik), a.err, 24,
-                           abort_flag);
-            if (!ok) break;
             tc_fence_after();
             if (j + 1 < n_kv0) {
               qk(0, ring_slot(ik));
-              tc_commit(smem_u32(&bars[kBarS + 0]));
+              if (leader) tc_commit(smem_u32(&bars[kBarS + 0]));
             }
           }
           ok = mbar_wait(smem_u32(&bars[kBarP + 1]), j & 1, a.err, 25, abort_flag);
           if (!ok) break;
           tc_fence_after();
           pv(1, ring_slot(iv), j > 0);
-          tc_commit(smem_u32(&bars[kBarEmpty + ring_slot(iv)]));
+          if (leader) tc_commit(smem_u32(&bars[kBarEmpty + ring_slot(iv)]));
           if (next) {
             qk(1, ring_slot(ik));
-            tc_commit(smem_u32(&bars[kBarS + 1]));
-            tc_commit(smem_u32(&bars[kBarEmpty + ring_slot(ik)]));
+            if (leader) tc_commit(smem_u32(&bars[kBarS + 1]));
+            if (leader) tc_commit(smem_u32(&bars[kBarEmpty + ring_slot(ik)]));
           }
         }
-        tc_commit(smem_u32(&bars[kBarO]));
+        if (leader) tc_commit(smem_u32(&bars[kBarO]));
       }
     }
   }

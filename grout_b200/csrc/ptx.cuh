@@ -136,6 +136,14 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// One lane of a converged warp (the same lane on every call).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t r;
+  asm volatile(
+      "{ .reg .pred p; .reg .b32 l; elect.sync l|p, 0xffffffff; selp.u32 %0, 1, 0, p; }"
+      : "=r"(r));
+  return r != 0;
+}
 // Arrive on an mbarrier once all previously issued tcgen05 async ops of
 // this thread have completed.
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
