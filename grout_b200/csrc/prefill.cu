@@ -5,19 +5,23 @@
 // (2462-2557): O = softmax(scale * Q K^T + causal mask) V per query head,
 // f16 in, f32 accumulate, P rounded to f16 before the PV product, f16 out.
 //
-// One CTA = two 128-row query tiles of one head (256 query rows), streaming
-// 128-key K/V tiles.  Warp roles (384 threads, 3 warpgroups):
-//   warps 0-3  softmax for query tile 0 (one thread per query row = TMEM lane)
-//   warps 4-7  softmax for query tile 1
-//   warp 8     TMA producer: Q tiles once, then K_j, V_j into a 4-slot ring
-//   warp 9     MMA issuer: the whole warp runs the issue loop (so its
-//              descriptors stay warp-uniform) and one elected lane issues
-//              every tcgen05.mma and tcgen05.commit.  This warp shares its
-//              SM sub-partition with two busy softmax warps, so each MMA is
-//              kept to a few instructions: descriptors are precomputed low
-//              words advanced by constant adds.
-//   warps 10-11 idle (they complete the third warpgroup, whose registers
-//              setmaxnreg hands to the softmax warpgroups)
+// Persistent kernel: one CTA per SM walks a list of work items; an item is
+// two 128-row query tiles of one (sequence, head), streaming 128-key K/V
+// tiles.  Warp roles (512 threads, 4 warpgroups):
+//   warps 0-3   softmax for query tile 0 (one thread per query row = TMEM lane)
+//   warps 4-7   softmax for query tile 1
+//   warps 8-11  output: read the finished O_t out of TMEM (warp 8 + q owns
+//               TMEM lanes 32q..), free it for the next item, normalise by
+//               the row sums and store the rows
+//   warp 12     TMA producer: Q_0, K_0, Q_1, V_0, K_1, ... of each item into
+//               two query buffers and a 4-slot K/V ring
+//   warp 13     MMA issuer: the whole warp runs the issue loop (so its
+//               descriptors stay warp-uniform) and one elected lane issues
+//               every tcgen05.mma and tcgen05.commit.  This warp shares its
+//               SM sub-partition with two busy softmax warps, so each MMA is
+//               kept to a few instructions: descriptors are precomputed low
+//               words advanced by constant adds.
+//   warps 14-15 idle (they complete the fourth warpgroup)
 // Tensor memory (512 columns, f32): S0 [0,128) S1 [128,256) O0 [256,384)
 // O1 [384,512).  P_t (f16 pairs) overwrites the first 64 columns of S_t and
 // feeds the PV MMA straight from TMEM (A operand in TMEM, V from shared
@@ -26,11 +30,11 @@
 // the next S of one query tile is computed while the other tile's softmax
 // runs.  Because tcgen05 operations of one thread complete in issue order,
 // "S_t(j+1) ready" also means "PV_t(j) done", which is what the softmax
-// warps need before they rescale O_t in place.
-// Scheduling: blockIdx.y walks query-tile pairs from the last (longest
-// causal row range) to the first, so the heaviest CTAs start first;
-// blockIdx.x is the query head, so the G heads that share a KV head run
-// side by side and reuse its K/V through L2.
+// warps need before they rescale O_t in place.  Each tile flows straight
+// into the next item (QK_t of item n+1 follows the last PV_t of item n, and
+// each query buffer is reloaded as soon as its tile's last QK has run), so
+// the half-period offset between the two tiles survives item boundaries and
+// the output of one item overlaps the start of the next.
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -42,25 +46,29 @@ constexpr int kBN = 128;          // keys per KV tile
 constexpr int kSlots = 4;         // K/V ring slots
 constexpr int kTile = 128 * 128 * 2;  // bytes of one 128x128 f16 tile (two 64-col boxes)
 constexpr int kBox = kTile / 2;
-constexpr int kThreads = 384;  // 3 warpgroups
-// Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512);
-// the producer/MMA warpgroup drops to 104, the two softmax warpgroups rise to
-// 192: 128 x 104 + 256 x 192 = 62464 <= 64512.
-constexpr int kRegsIssue = 104;
+constexpr int kThreads = 512;     // 4 warpgroups, one persistent CTA per SM
+// Register split (setmaxnreg): launched at 128 per thread (512 x 128 =
+// 65536); the two softmax warpgroups rise to 192, the output and issue
+// warpgroups drop to 64: 2 x 128 x 192 + 2 x 128 x 64 = 65536.
+constexpr int kRegsOther = 64;
 constexpr int kRegsSoftmax = 192;
 constexpr int kOffQ = 0;                       // 2 query tiles
 constexpr int kOffKV = 2 * kTile;              // ring
 constexpr int kOffBar = kOffKV + kSlots * kTile;
-constexpr int kSmemBytes = kOffBar + 256 + 1024;
+constexpr int kOffL = kOffBar + 512;           // row sums [item parity][tile][row]
+constexpr int kSmemBytes = kOffL + 2 * 2 * 128 * 4 + 1024;
 
-// barrier indices
-constexpr int kBarQ = 0;
-constexpr int kBarFull = 1;                 // + slot
+// barrier indices (phases run on across the work items of a CTA)
+constexpr int kBarQ = 0;                      // + tile: Q_t landed (TMA)
+constexpr int kBarQfree = 2;                  // + tile: last QK_t of the item done (commit)
+constexpr int kBarFull = 4;                   // + slot
 constexpr int kBarEmpty = kBarFull + kSlots;  // + slot
-constexpr int kBarS = kBarEmpty + kSlots;   // + tile
-constexpr int kBarP = kBarS + 2;            // + tile
-constexpr int kBarO = kBarP + 2;
-constexpr int kNumBars = kBarO + 1;
+constexpr int kBarS = kBarEmpty + kSlots;     // + tile (commit)
+constexpr int kBarP = kBarS + 2;              // + tile (4 softmax warps)
+constexpr int kBarOfull = kBarP + 2;          // + tile: O_t of the item final (commit)
+constexpr int kBarOempty = kBarOfull + 2;     // + tile: O_t read out (4 output warps)
+constexpr int kBarL = kBarOempty + 2;         // + tile: row sums written (4 softmax warps)
+constexpr int kNumBars = kBarL + 2;
 
 // ---- packed f32x2 arithmetic (sm_100a): two softmax elements per instruction
 __device__ __forceinline__ uint64_t f2pack(float a, float b) {
@@ -152,6 +160,38 @@ __device__ __forceinline__ void mma_ts_lo(uint32_t d, uint32_t a_tmem, uint32_t 
       : "memory");
 }
 
+// One work item = two 128-row query tiles of one (sequence, head); items are
+// numbered longest-first (query-tile pair descending, then head, then
+// sequence).  In round r CTA c takes item r * gridDim.x + c, or
+// r * gridDim.x + gridDim.x - 1 - c in odd rounds: the snake order evens out
+// the causal work per CTA (a plain stride leaves the first CTAs ~12% more).
+struct Item {
+  int h, b, q0, S, P, ks, q_start, n_kv, n_kv0;
+};
+__device__ __forceinline__ bool decode_item(const PrefillArgs& a, int idx, int n_pairs, Item& it) {
+  const int per = a.hq * a.batch;
+  const int pair = n_pairs - 1 - idx / per;
+  const int rem = idx - (idx / per) * per;
+  it.h = rem % a.hq;
+  it.b = rem / a.hq;
+  if (a.cu_q) {
+    it.q_start = a.cu_q[it.b];
+    it.S = a.cu_q[it.b + 1] - it.q_start;
+  } else {
+    it.q_start = 0;
+    it.S = a.single_len;
+  }
+  it.P = a.pos0 ? a.pos0[it.b] : a.single_pos0;
+  it.ks = a.kv_start ? a.kv_start[it.b] : 0;
+  it.q0 = pair * 2 * kBM;
+  if (it.q0 >= it.S) return false;  // ragged batch: this sequence is shorter
+  const int rows_hi = min(it.q0 + 2 * kBM, it.S);
+  it.n_kv = (it.P + rows_hi + kBN - 1) / kBN;
+  // query tile 0 (rows q0 .. q0+127) never sees keys beyond P + q0 + 127
+  it.n_kv0 = (it.P + min(it.q0 + kBM, it.S) + kBN - 1) / kBN;
+  return true;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
@@ -161,44 +201,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* lbuf = reinterpret_cast<float*>(smem + kOffL);
 
-  const int h = blockIdx.x;
-  const int b = blockIdx.z;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  int q_start, S, P, ks;
-  if (a.cu_q) {
-    q_start = a.cu_q[b];
-    S = a.cu_q[b + 1] - q_start;
-  } else {
-    q_start = 0;
-    S = a.single_len;
-  }
-  P = a.pos0 ? a.pos0[b] : a.single_pos0;
-  ks = a.kv_start ? a.kv_start[b] : 0;
   const int n_pairs = (a.max_q_len + 2 * kBM - 1) / (2 * kBM);
-  const int pair = n_pairs - 1 - (int)blockIdx.y;
-  const int q0 = pair * 2 * kBM;
-  if (q0 >= S) return;  // ragged batch: this sequence is shorter
-  const int rows_hi = min(q0 + 2 * kBM, S);
-  const int kv_len = P + S;
-  const int n_kv = (P + rows_hi + kBN - 1) / kBN;
-  // query tile 0 (rows q0 .. q0+127) never sees keys beyond P + q0 + 127
-  const int n_kv0 = (P + min(q0 + kBM, S) + kBN - 1) / kBN;
-  const int kh = h / (a.hq / a.hkv);
-  const int kvb = a.kv_batched ? b : 0;
+  const int n_items = n_pairs * a.hq * a.batch;
+  auto item_of = [&](int r) {
+    return r * (int)gridDim.x + ((r & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x);
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i) {
       uint32_t cnt = 1;
-      if (i == kBarP || i == kBarP + 1) cnt = kBM;
+      if ((i >= kBarP && i < kBarP + 2) || (i >= kBarOempty && i < kBarOempty + 2) ||
+          (i >= kBarL && i < kBarL + 2))
+        cnt = 4;  // one arrival per warp of a warpgroup
       mbar_init(smem_u32(&bars[i]), cnt);
     }
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 9) {
+  if (warp == 13) {
     tmem_alloc(smem_u32(tmem_holder), 512);
     tmem_relinquish();
   }
@@ -209,119 +233,245 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t smem_base = smem_u32(smem);
 
   if (warp >= 8) {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsIssue));
-  if (warp == 8) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsOther));
+  if (warp == 12) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_k);
       prefetch_tmap(&tm_v);
-      const uint32_t bq = smem_u32(&bars[kBarQ]);
-      mbar_arrive_expect_tx(bq, 2 * kTile);
-      for (int t = 0; t < 2; ++t) {
-        const uint32_t dst = smem_base + kOffQ + t * kTile;
-        const int row = q_start + q0 + t * kBM;
-        tma_load_3d(dst, &tm_q, bq, 0, h, row);
-        tma_load_3d(dst + kBox, &tm_q, bq, 64, h, row);
-      }
-      for (int i = 0; i < 2 * n_kv; ++i) {
-        const int slot = ring_slot(i);
-        if (i >= kSlots &&
-            !mbar_wait(smem_u32(&bars[kBarEmpty + slot]), ring_parity(i) ^ 1u, a.err, 10,
-                       abort_flag))
-          break;
-        const uint32_t full = smem_u32(&bars[kBarFull + slot]);
-        mbar_arrive_expect_tx(full, kTile);
-        const CUtensorMap* map = (i & 1) ? &tm_v : &tm_k;
-        const uint32_t dst = smem_base + kOffKV + slot * kTile;
-        const int row = ks + (i >> 1) * kBN;
-        if (a.kv_batched) {
-          tma_load_4d(dst, map, full, 0, row, kh, kvb);
-          tma_load_4d(dst + kBox, map, full, 64, row, kh, kvb);
-        } else {
-          tma_load_3d(dst, map, full, 0, row, kh);
-          tma_load_3d(dst + kBox, map, full, 64, row, kh);
+      int ring = 0, nq = 0;
+      bool ok = true;
+      for (int r = 0, idx; ok && (idx = item_of(r)) < n_items; ++r) {
+        Item it;
+        if (!decode_item(a, idx, n_pairs, it)) continue;
+        const int kh = it.h / (a.hq / a.hkv);
+        const int kvb = a.kv_batched ? it.b : 0;
+        // Q_0, K_0, Q_1, then the rest: each tile's query buffer is refilled
+        // as soon as that tile's last QK of the previous item has run.
+        auto load_q = [&](int t) -> bool {
+          if (nq > 0 &&
+              !mbar_wait(smem_u32(&bars[kBarQfree + t]), (nq - 1) & 1, a.err, 11 + t, abort_flag))
+            return false;
+          const uint32_t bq = smem_u32(&bars[kBarQ + t]);
+          mbar_arrive_expect_tx(bq, kTile);
+          const uint32_t dst = smem_base + kOffQ + t * kTile;
+          const int row = it.q_start + it.q0 + t * kBM;
+          tma_load_3d(dst, &tm_q, bq, 0, it.h, row);
+          tma_load_3d(dst + kBox, &tm_q, bq, 64, it.h, row);
+          return true;
+        };
+        if (!load_q(0)) break;
+        for (int i = 0; i < 2 * it.n_kv; ++i, ++ring) {
+          if (i == 1 && !load_q(1)) {
+            ok = false;
+            break;
+          }
+          const int slot = ring_slot(ring);
+          if (ring >= kSlots &&
+              !mbar_wait(smem_u32(&bars[kBarEmpty + slot]), ring_parity(ring) ^ 1u, a.err, 10,
+                         abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full = smem_u32(&bars[kBarFull + slot]);
+          mbar_arrive_expect_tx(full, kTile);
+          const CUtensorMap* map = (i & 1) ? &tm_v : &tm_k;
+          const uint32_t dst = smem_base + kOffKV + slot * kTile;
+          const int row = it.ks + (i >> 1) * kBN;
+          if (a.kv_batched) {
+            tma_load_4d(dst, map, full, 0, row, kh, kvb);
+            tma_load_4d(dst + kBox, map, full, 64, row, kh, kvb);
+          } else {
+            tma_load_3d(dst, map, full, 0, row, kh);
+            tma_load_3d(dst + kBox, map, full, 64, row, kh);
+          }
         }
+        ++nq;
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == 13) {
     // ------------------------------------------------------------- MMA issue
     // The whole warp runs the issue loop (warp-uniform descriptors); one
-    // elected lane issues every MMA and commit.
-    {
-      const bool leader = elect_one();
-      constexpr uint32_t idesc_qk = idesc_f16_f32(kBM, kBN, 0, 0);
-      constexpr uint32_t idesc_pv = idesc_f16_f32(kBM, 128, 0, 1);
-      // Shared-memory descriptors as (low word, constant high word): the
-      // start-address field of the low word is advanced by plain adds (all
-      // addresses are below 256 KB, so the 14-bit field never carries).
-      const uint32_t base16 = smem_base >> 4;
-      auto qk = [&](int t, int slot) {
-        const uint32_t qlo = base16 + (kOffQ + t * kTile) / 16 + kDescLboK;
-        const uint32_t klo = base16 + (kOffKV + slot * kTile) / 16 + kDescLboK;
+    // elected lane issues every MMA and commit.  Per KV tile j of an item:
+    // PV0(j), QK0(j+1), PV1(j), QK1(j+1); the first QKs of the next item
+    // follow the last PVs of this one, and its first PV_t waits until the
+    // output warps have read O_t of this item out of TMEM.
+    const bool leader = elect_one();
+    constexpr uint32_t idesc_qk = idesc_f16_f32(kBM, kBN, 0, 0);
+    constexpr uint32_t idesc_pv = idesc_f16_f32(kBM, 128, 0, 1);
+    const uint32_t base16 = smem_base >> 4;
+    auto qk = [&](int t, int slot) {
+      const uint32_t qlo = base16 + (kOffQ + t * kTile) / 16 + kDescLboK;
+      const uint32_t klo = base16 + (kOffKV + slot * kTile) / 16 + kDescLboK;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = ((kk >> 2) * kBox + (kk & 3) * 32) / 16;
-          if (leader) mma_ss_lo(tmem + t * 128, qlo + off, klo + off, idesc_qk, kk > 0 ? 1u : 0u);
-        }
-      };
-      auto pv = [&](int t, int slot, bool acc) {
-        const uint32_t vlo = base16 + (kOffKV + slot * kTile) / 16 + kDescLboV;
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = ((kk >> 2) * kBox + (kk & 3) * 32) / 16;
+        if (leader) mma_ss_lo(tmem + t * 128, qlo + off, klo + off, idesc_qk, kk > 0 ? 1u : 0u);
+      }
+    };
+    auto pv = [&](int t, int slot, bool acc) {
+      const uint32_t vlo = base16 + (kOffKV + slot * kTile) / 16 + kDescLboV;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          if (leader) mma_ts_lo(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, vlo + kk * (2048 / 16), idesc_pv,
-                                (acc || kk > 0) ? 1u : 0u);
-        }
-      };
-      bool ok = mbar_wait(smem_u32(&bars[kBarQ]), 0, a.err, 20, abort_flag);
-      ok = ok && mbar_wait(smem_u32(&bars[kBarFull + ring_slot(0)]), ring_parity(0), a.err, 21,
-                           abort_flag);
+      for (int kk = 0; kk < 8; ++kk) {
+        if (leader) mma_ts_lo(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, vlo + kk * (2048 / 16), idesc_pv,
+                              (acc || kk > 0) ? 1u : 0u);
+      }
+    };
+    // Each tile runs on into the next item: right after tile t's last PV of
+    // item n the warp issues QK_t of item n + 1, so the two tiles keep their
+    // half-period offset across item boundaries.
+    auto next_valid = [&](int& rr, Item& itm) -> bool {
+      for (int idx; (idx = item_of(rr)) < n_items; ++rr)
+        if (decode_item(a, idx, n_pairs, itm)) return true;
+      return false;
+    };
+    int ring = 0, nq = 0, pc0 = 0, pc1 = 0;
+    int rr = 0;
+    Item cur;
+    bool has = next_valid(rr, cur);
+    bool ok = true;
+    if (has) {
+      ok = mbar_wait(smem_u32(&bars[kBarQ + 0]), 0, a.err, 20, abort_flag) &&
+           mbar_wait(smem_u32(&bars[kBarFull + ring_slot(ring)]), ring_parity(ring), a.err, 21, abort_flag);
       if (ok) {
         tc_fence_after();
-        qk(0, ring_slot(0));
+        qk(0, ring_slot(ring));
         if (leader) tc_commit(smem_u32(&bars[kBarS + 0]));
-        qk(1, ring_slot(0));
+        if (cur.n_kv0 == 1 && leader) tc_commit(smem_u32(&bars[kBarQfree + 0]));
+        ok = mbar_wait(smem_u32(&bars[kBarQ + 1]), 0, a.err, 28, abort_flag);
+      }
+      if (ok) {
+        tc_fence_after();
+        qk(1, ring_slot(ring));
         if (leader) tc_commit(smem_u32(&bars[kBarS + 1]));
-        if (leader) tc_commit(smem_u32(&bars[kBarEmpty + ring_slot(0)]));
-        for (int j = 0; j < n_kv && ok; ++j) {
-          const int iv = 2 * j + 1, ik = 2 * j + 2;
-          const bool next = j + 1 < n_kv;
-          ok = mbar_wait(smem_u32(&bars[kBarFull + ring_slot(iv)]), ring_parity(iv), a.err, 22,
+        if (leader) tc_commit(smem_u32(&bars[kBarEmpty + ring_slot(ring)]));
+        if (cur.n_kv == 1 && leader) tc_commit(smem_u32(&bars[kBarQfree + 1]));
+      }
+    }
+    while (has && ok) {
+      int rn = rr + 1;
+      Item nx;
+      const bool hn = next_valid(rn, nx);
+      const int n_kv = cur.n_kv, n_kv0 = cur.n_kv0;
+      const int nring = ring + 2 * n_kv;  // K_0 of the next item
+      for (int j = 0; j < n_kv; ++j) {
+        const int iv = ring + 2 * j + 1, ik = ring + 2 * j + 2;
+        const bool next = j + 1 < n_kv;
+        ok = mbar_wait(smem_u32(&bars[kBarFull + ring_slot(iv)]), ring_parity(iv), a.err, 22, abort_flag);
+        // K(j+1) only needs the slot K(j-1) released, so it is awaited
+        // here, before P0(j), keeping the wait off the PV0 -> QK0 path.
+        if (ok && next)
+          ok = mbar_wait(smem_u32(&bars[kBarFull + ring_slot(ik)]), ring_parity(ik), a.err, 24, abort_flag);
+        if (!ok) break;
+        if (j < n_kv0) {
+          ok = mbar_wait(smem_u32(&bars[kBarP + 0]), pc0 & 1, a.err, 23, abort_flag);
+          if (ok && j == 0 && nq > 0)
+            ok = mbar_wait(smem_u32(&bars[kBarOempty + 0]), (nq - 1) & 1, a.err, 26, abort_flag);
+          if (!ok) break;
+          ++pc0;
+          tc_fence_after();
+          pv(0, ring_slot(iv), j > 0);
+          if (j == n_kv0 - 1 && leader) tc_commit(smem_u32(&bars[kBarOfull + 0]));
+        }
+        if (j + 1 < n_kv0) {
+          tc_fence_after();
+          qk(0, ring_slot(ik));
+          if (leader) tc_commit(smem_u32(&bars[kBarS + 0]));
+          if (j + 1 == n_kv0 - 1 && leader) tc_commit(smem_u32(&bars[kBarQfree + 0]));
+        } else if (j + 1 == n_kv0 && hn) {
+          // tile 0 is done with this item: start the next one
+          ok = mbar_wait(smem_u32(&bars[kBarQ + 0]), (nq + 1) & 1, a.err, 20, abort_flag) &&
+               mbar_wait(smem_u32(&bars[kBarFull + ring_slot(nring)]), ring_parity(nring), a.err, 21,
                          abort_flag);
           if (!ok) break;
-          // K(j+1) only needs the slot K(j-1) released, so it is awaited
-          // here, before P0(j), keeping the wait off the PV0 -> QK0 path.
-          if (next) {
-            ok = mbar_wait(smem_u32(&bars[kBarFull + ring_slot(ik)]), ring_parity(ik), a.err, 24,
-                           abort_flag);
-            if (!ok) break;
-          }
-          if (j < n_kv0) {
-            ok = mbar_wait(smem_u32(&bars[kBarP + 0]), j & 1, a.err, 23, abort_flag);
-            if (!ok) break;
-            tc_fence_after();
-            pv(0, ring_slot(iv), j > 0);
-          }
-          if (next) {
-            tc_fence_after();
-            if (j + 1 < n_kv0) {
-              qk(0, ring_slot(ik));
-              if (leader) tc_commit(smem_u32(&bars[kBarS + 0]));
-            }
-          }
-          ok = mbar_wait(smem_u32(&bars[kBarP + 1]), j & 1, a.err, 25, abort_flag);
+          tc_fence_after();
+          qk(0, ring_slot(nring));
+          if (leader) tc_commit(smem_u32(&bars[kBarS + 0]));
+          if (nx.n_kv0 == 1 && leader) tc_commit(smem_u32(&bars[kBarQfree + 0]));
+        }
+        ok = mbar_wait(smem_u32(&bars[kBarP + 1]), pc1 & 1, a.err, 25, abort_flag);
+        if (ok && j == 0 && nq > 0)
+          ok = mbar_wait(smem_u32(&bars[kBarOempty + 1]), (nq - 1) & 1, a.err, 27, abort_flag);
+        if (!ok) break;
+        ++pc1;
+        tc_fence_after();
+        pv(1, ring_slot(iv), j > 0);
+        if (leader) tc_commit(smem_u32(&bars[kBarEmpty + ring_slot(iv)]));
+        if (!next && leader) tc_commit(smem_u32(&bars[kBarOfull + 1]));
+        if (next) {
+          qk(1, ring_slot(ik));
+          if (leader) tc_commit(smem_u32(&bars[kBarS + 1]));
+          if (leader) tc_commit(smem_u32(&bars[kBarEmpty + ring_slot(ik)]));
+          if (j + 1 == n_kv - 1 && leader) tc_commit(smem_u32(&bars[kBarQfree + 1]));
+        } else if (hn) {
+          // tile 1 is done with this item: start the next one (K_0 of it
+          // was awaited when tile 0 started it)
+          ok = mbar_wait(smem_u32(&bars[kBarQ + 1]), (nq + 1) & 1, a.err, 28, abort_flag);
           if (!ok) break;
           tc_fence_after();
-          pv(1, ring_slot(iv), j > 0);
-          if (leader) tc_commit(smem_u32(&bars[kBarEmpty + ring_slot(iv)]));
-          if (next) {
-            qk(1, ring_slot(ik));
-            if (leader) tc_commit(smem_u32(&bars[kBarS + 1]));
-            if (leader) tc_commit(smem_u32(&bars[kBarEmpty + ring_slot(ik)]));
+          qk(1, ring_slot(nring));
+          if (leader) tc_commit(smem_u32(&bars[kBarS + 1]));
+          if (leader) tc_commit(smem_u32(&bars[kBarEmpty + ring_slot(nring)]));
+          if (nx.n_kv == 1 && leader) tc_commit(smem_u32(&bars[kBarQfree + 1]));
+        }
+      }
+      if (!ok) break;
+      ring = nring;
+      ++nq;
+      cur = nx;
+      rr = rn;
+      has = hn;
+    }
+  } else if (warp < 12) {
+    // ------------------------------------------------------------ output
+    // Warp 8 + q reads TMEM lanes 32q.. (query rows) of O_t once the MMA
+    // warp reports it final, frees O_t for the next item, and writes the
+    // normalised rows.
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    int nq = 0;
+    bool ok = true;
+    for (int r = 0, idx; ok && (idx = item_of(r)) < n_items; ++r) {
+      Item it;
+      if (!decode_item(a, idx, n_pairs, it)) continue;
+#pragma unroll 1
+      for (int t = 0; t < 2; ++t) {
+        ok = mbar_wait(smem_u32(&bars[kBarOfull + t]), nq & 1, a.err, 40 + t, abort_flag);
+        ok = ok && mbar_wait(smem_u32(&bars[kBarL + t]), nq & 1, a.err, 42 + t, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        const float inv_l = 1.0f / fmaxf(lbuf[((nq & 1) * 2 + t) * 128 + row], 1.0e-8f);
+        const int row_q = it.q0 + t * kBM + row;
+        const bool valid = row_q < it.S;
+        __half* orow = a.out + (int64_t)(it.q_start + row_q) * a.q_row_stride + (int64_t)it.h * 128;
+        const uint32_t tO = tmem + 256 + t * 128 + lane_off;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tO + c * 32, r);
+          tc_wait_ld();
+          if (c == 3) {  // all of O_t is in registers now: release it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&bars[kBarOempty + t]));
+          }
+          if (valid) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 u;
+              u.x = pack_half2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
+              u.y = pack_half2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
+              u.z = pack_half2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
+              u.w = pack_half2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
+              dst[v] = u;
+            }
           }
         }
-        if (leader) tc_commit(smem_u32(&bars[kBarO]));
       }
+      ++nq;
     }
   }
   } else {
@@ -332,129 +482,124 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + t * 128 + lane_off;
     const uint32_t tO = tmem + 256 + t * 128 + lane_off;
-    const int row_q = q0 + t * kBM + row;
-    const int key_lim = min(P + row_q, kv_len - 1);  // last visible key
     const float sl2 = a.scale_log2;
-    const int n_t = t == 0 ? n_kv0 : n_kv;
-    float m_run = -INFINITY, l = 0.f;  // m_run: the max P is exponentiated against
+    int sc = 0, nq = 0;
     bool ok = true;
-    for (int j = 0; j < n_t; ++j) {
-      ok = mbar_wait(smem_u32(&bars[kBarS + t]), j & 1, a.err, 30 + t, abort_flag);
-      if (!ok) break;
-      tc_fence_after();
-      uint32_t r[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, r[c]);
-      tc_wait_ld();
-      float s[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[c][i]);
-      const int lim = key_lim - j * kBN;
-      if (lim < kBN - 1) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (c > lim) s[c] = -INFINITY;
-      }
-      float mx0 = fmaxf(s[0], s[1]), mx1 = fmaxf(s[2], s[3]);
-      float mx2 = fmaxf(s[4], s[5]), mx3 = fmaxf(s[6], s[7]);
-#pragma unroll
-      for (int c = 8; c < 128; c += 8) {
-        mx0 = fmax3(mx0, s[c], s[c + 1]);
-        mx1 = fmax3(mx1, s[c + 2], s[c + 3]);
-        mx2 = fmax3(mx2, s[c + 4], s[c + 5]);
-        mx3 = fmax3(mx3, s[c + 6], s[c + 7]);
-      }
-      const float mx_s = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
-      float alpha = 1.0f;
-      float m_new = m_run;
-      if (mx_s > m_run + kRescaleThreshold) {
-        m_new = mx_s;
-        alpha = ex2(m_run - m_new);
-      }
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const uint64_t sl2x2 = f2pack(sl2, sl2);
-      const uint64_t negm2 = f2pack(-m_use, -m_use);
-      uint64_t rsum = f2pack(0.f, 0.f);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const uint64_t x2 = ffma2(f2pack(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1]), sl2x2, negm2);
-          float p0, p1;
-          if (poly_pair(i)) {
-            ex2_poly2(x2, p0, p1);
-          } else {
-            float x0, x1;
-            f2unpack(x2, x0, x1);
-            p0 = ex2(x0);
-            p1 = ex2(x1);
-          }
-          rsum = fadd2(rsum, f2pack(p0, p1));
-          pk[i] = pack_half2(p0, p1);
-        }
-        asm volatile(
-            "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, "
-            "%10, %11, %12, %13, %14, %15, %16};" ::"r"(tS + c * 16),
-            "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3]), "r"(pk[4]), "r"(pk[5]), "r"(pk[6]),
-            "r"(pk[7]), "r"(pk[8]), "r"(pk[9]), "r"(pk[10]), "r"(pk[11]), "r"(pk[12]),
-            "r"(pk[13]), "r"(pk[14]), "r"(pk[15])
-            : "memory");
-      }
-      float rs0, rs1;
-      f2unpack(rsum, rs0, rs1);
-      l = l * alpha + (rs0 + rs1);
-      // Rescale O_t only when some row of the warp moved its reference max
-      // (PV_t(j-1) has completed: it was issued before the QK that produced
-      // this S).
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + c * 32, o);
-          tc_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(tO + c * 32, o);
-        }
-      }
-      tc_wait_st();
-      tc_fence_before();
-      mbar_arrive(smem_u32(&bars[kBarP + t]));
-      m_run = m_new;
-    }
-    if (ok) ok = mbar_wait(smem_u32(&bars[kBarO]), 0, a.err, 40, abort_flag);
-    if (ok) {
-      tc_fence_after();
-      const float inv_l = 1.0f / fmaxf(l, 1.0e-8f);
-      const bool valid = row_q < S;
-      __half* orow = a.out + (int64_t)(q_start + row_q) * a.q_row_stride + (int64_t)h * 128;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tO + c * 32, r);
+    for (int r = 0, idx; ok && (idx = item_of(r)) < n_items; ++r) {
+      Item it;
+      if (!decode_item(a, idx, n_pairs, it)) continue;
+      const int row_q = it.q0 + t * kBM + row;
+      const int kv_len = it.P + it.S;
+      const int key_lim = min(it.P + row_q, kv_len - 1);  // last visible key
+      const int n_t = t == 0 ? it.n_kv0 : it.n_kv;
+      float m_run = -INFINITY, l = 0.f;  // m_run: the max P is exponentiated against
+      for (int j = 0; j < n_t; ++j) {
+        ok = mbar_wait(smem_u32(&bars[kBarS + t]), sc & 1, a.err, 30 + t, abort_flag);
+        if (!ok) break;
+        ++sc;
+        tc_fence_after();
+        uint32_t r[4][32];
+  #pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, r[c]);
         tc_wait_ld();
-        if (valid) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 u;
-            u.x = pack_half2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
-            u.y = pack_half2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
-            u.z = pack_half2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
-            u.w = pack_half2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
-            dst[v] = u;
+        float s[128];
+  #pragma unroll
+        for (int c = 0; c < 4; ++c)
+  #pragma unroll
+          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[c][i]);
+        const int lim = key_lim - j * kBN;
+        if (lim < kBN - 1) {
+  #pragma unroll
+          for (int c = 0; c < 128; ++c)
+            if (c > lim) s[c] = -INFINITY;
+        }
+        float mx0 = fmaxf(s[0], s[1]), mx1 = fmaxf(s[2], s[3]);
+        float mx2 = fmaxf(s[4], s[5]), mx3 = fmaxf(s[6], s[7]);
+  #pragma unroll
+        for (int c = 8; c < 128; c += 8) {
+          mx0 = fmax3(mx0, s[c], s[c + 1]);
+          mx1 = fmax3(mx1, s[c + 2], s[c + 3]);
+          mx2 = fmax3(mx2, s[c + 4], s[c + 5]);
+          mx3 = fmax3(mx3, s[c + 6], s[c + 7]);
+        }
+        const float mx_s = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+        float alpha = 1.0f;
+        float m_new = m_run;
+        if (mx_s > m_run + kRescaleThreshold) {
+          m_new = mx_s;
+          alpha = ex2(m_run - m_new);
+        }
+        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+        const uint64_t sl2x2 = f2pack(sl2, sl2);
+        const uint64_t negm2 = f2pack(-m_use, -m_use);
+        uint64_t rsum = f2pack(0.f, 0.f);
+  #pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
+  #pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const uint64_t x2 = ffma2(f2pack(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1]), sl2x2, negm2);
+            float p0, p1;
+            if (poly_pair(i)) {
+              ex2_poly2(x2, p0, p1);
+            } else {
+              float x0, x1;
+              f2unpack(x2, x0, x1);
+              p0 = ex2(x0);
+              p1 = ex2(x1);
+            }
+            rsum = fadd2(rsum, f2pack(p0, p1));
+            pk[i] = pack_half2(p0, p1);
+          }
+          asm volatile(
+              "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, "
+              "%10, %11, %12, %13, %14, %15, %16};" ::"r"(tS + c * 16),
+              "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3]), "r"(pk[4]), "r"(pk[5]), "r"(pk[6]),
+              "r"(pk[7]), "r"(pk[8]), "r"(pk[9]), "r"(pk[10]), "r"(pk[11]), "r"(pk[12]),
+              "r"(pk[13]), "r"(pk[14]), "r"(pk[15])
+              : "memory");
+        }
+        float rs0, rs1;
+        f2unpack(rsum, rs0, rs1);
+        l = l * alpha + (rs0 + rs1);
+        // Rescale O_t only when some row of the warp moved its reference max
+        // (PV_t(j-1) has completed: it was issued before the QK that produced
+        // this S).
+        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+  #pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tc_wait_ld();
+  #pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(tO + c * 32, o);
           }
         }
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&bars[kBarP + t]));
+        m_run = m_new;
       }
+      if (!ok) break;
+      // Row sums for the output warps.  The output warps must have taken
+      // the previous item's sums (O_t of that item read out) first, so the
+      // row-sum barrier never runs two phases ahead of its reader.
+      if (nq > 0) {
+        ok = mbar_wait(smem_u32(&bars[kBarOempty + t]), (nq - 1) & 1, a.err, 32 + t, abort_flag);
+        if (!ok) break;
+      }
+      lbuf[((nq & 1) * 2 + t) * 128 + row] = l;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars[kBarL + t]));
+      ++nq;
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 13) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -470,8 +615,17 @@ cudaError_t prefill_set_attributes() {
 cudaError_t launch_prefill(const PrefillArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                            const CUtensorMap& tm_v, cudaStream_t s) {
   const int n_pairs = (a.max_q_len + 2 * kBM - 1) / (2 * kBM);
-  if (n_pairs == 0 || a.batch == 0) return cudaSuccess;
-  dim3 grid(a.hq, n_pairs, a.batch);
+  const long long n_items = (long long)n_pairs * a.hq * a.batch;
+  if (n_items == 0) return cudaSuccess;
+  static int num_sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (num_sms[dev] == 0) {
+    cudaError_t e = cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+  }
+  const int grid = (int)(n_items < num_sms[dev] ? n_items : num_sms[dev]);
   prefill_kernel<<<grid, kThreads, kSmemBytes, s>>>(tm_q, tm_k, tm_v, a);
   return cudaGetLastError();
 }
