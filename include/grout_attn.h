@@ -136,7 +136,10 @@ grout_status grout_qk_norm_rope_kv_decode(const void* qkv, const void* q_norm_w,
  *   q, out [seq_len][num_q_heads][128] (contiguous),
  *   k_cache, v_cache [num_kv_heads][max_seq][128] (head stride cache_head_stride),
  *   query row m (position position_start + m) attends to cache keys
- *   0 .. position_start + m.  Scale dims->qk_scale (f32; default 1/sqrt(128)). */
+ *   0 .. position_start + m.  Scale dims->qk_scale (f32; default 1/sqrt(128)).
+ * The kernel is persistent: min(work items, SM count) CTAs of 512 threads and
+ * ~200 KB of shared memory each, so it occupies every SM until it finishes
+ * (kernels on other streams do not overlap with it). */
 grout_status grout_attn_prefill(const void* q, const void* k_cache, const void* v_cache,
                                 void* out, int64_t cache_head_stride, int32_t position_start,
                                 int32_t seq_len, const grout_attn_dims* dims,
