@@ -8,6 +8,7 @@ and the build script (build.py).
 from .attn import (  # noqa: F401
     GroutError,
     attention_decode,
+    attention_decode_paged,
     attention_prefill,
     attention_prefill_varlen,
     check_device_error,
@@ -17,7 +18,9 @@ from .attn import (  # noqa: F401
     inv_freq,
     lib,
     qk_norm_rope_kv_decode,
+    qk_norm_rope_kv_decode_paged,
     qk_norm_rope_kv_prefill,
+    qk_norm_rope_kv_prefill_paged,
     rope_table,
 )
 

@@ -104,6 +104,13 @@ SIGNATURES = {
     "grout_attn_decode_noalloc_max_bytes": (_sz, []),
     "grout_attn_decode_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i32, _i32,
                                                  _DIMS, _vp]),
+    "grout_attn_decode_paged": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _vp, _i32, _vp, _vp, _i32,
+                                               _i32, _i32, _DIMS, _vp, _sz, _vp]),
+    "grout_qk_norm_rope_kv_decode_paged": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32,
+                                                          _i32, _vp, _i32, _vp, _i32, _DIMS, _vp]),
+    "grout_qk_norm_rope_kv_prefill_paged": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp,
+                                                           _vp, _vp, _vp, _i32, _i32, _vp, _i32, _i32,
+                                                           _DIMS, _vp]),
 }
 
 _lib = None
@@ -343,6 +350,100 @@ def attention_decode(q, k_cache, v_cache, position, out, max_kv_len, workspace=N
         _ptr(position), _ptr(out), B, int(max_kv_len), int(num_splits), ctypes.byref(dims),
         _ptr(workspace), ws_bytes, _stream(q)))
     return out
+
+
+def _pages(k_pages, v_pages, page_table):
+    for t, n in ((k_pages, "k_pages"), (v_pages, "v_pages")):
+        _f16_cuda(t, n)
+    _need(k_pages.dim() == 4 and k_pages.shape[3] == HEAD_DIM,
+          f"k_pages must be [num_pages, Hkv, page_size, 128]: {tuple(k_pages.shape)}")
+    _need(v_pages.shape == k_pages.shape, "v_pages shape mismatch")
+    _need(page_table.is_cuda and page_table.dtype == torch.int32 and page_table.is_contiguous(),
+          "page_table must be a contiguous device int32 tensor")
+    return k_pages.shape[0], k_pages.shape[1], k_pages.shape[2]
+
+
+def attention_decode_paged(q, k_pages, v_pages, page_table, position, out, max_kv_len,
+                           max_seq=None, workspace=None, num_splits=None, qk_scale=None,
+                           scale_f16=True):
+    """Split-K GQA decode over a paged cache.  q, out [B, Hq, 128]; page pools
+    [num_pages, Hkv, page_size, 128]; page_table [B, table_stride] int32
+    (position p of sequence b is row p % page_size of page
+    page_table[b, p // page_size]); position [B] device int32/uint32.
+    max_seq defaults to table_stride * page_size."""
+    for t, n in ((q, "q"), (out, "out")):
+        _f16_cuda(t, n)
+    num_pages, hkv, page_size = _pages(k_pages, v_pages, page_table)
+    B, hq = q.shape[0], q.shape[1]
+    _need(out.shape == q.shape, "out shape mismatch")
+    _need(page_table.dim() == 2 and page_table.shape[0] >= B, "page_table must be [B, table_stride]")
+    _need(position.is_cuda and position.dtype in (torch.int32, torch.uint32) and position.numel() >= B,
+          "position must be a device int32/uint32 tensor with one entry per sequence")
+    stride = page_table.shape[1]
+    if max_seq is None:
+        max_seq = stride * page_size
+    dims = make_dims(hq, hkv, int(max_seq), qk_scale=qk_scale,
+                     flags=FLAG_DECODE_SCALE_F16 if scale_f16 else 0)
+    if num_splits is None:
+        num_splits = lib().grout_attn_decode_splits(B, int(max_kv_len), ctypes.byref(dims))
+    need = decode_workspace_bytes(B, max_kv_len, hq, hkv, int(max_seq), num_splits)
+    if need and workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    _check(lib().grout_attn_decode_paged(
+        _ptr(q), _ptr(k_pages), _ptr(v_pages), num_pages, page_size, _ptr(page_table), stride,
+        _ptr(position), _ptr(out), B, int(max_kv_len), int(num_splits), ctypes.byref(dims),
+        _ptr(workspace), ws_bytes, _stream(q)))
+    return out
+
+
+def qk_norm_rope_kv_decode_paged(qkv, q_norm_w, k_norm_w, rope_table, q_out, k_pages, v_pages,
+                                 page_table, position, num_q_heads, num_kv_heads, eps,
+                                 max_seq=None):
+    """Fused decode step writing K/V into a paged cache (see
+    attention_decode_paged for the layout)."""
+    for t, n in ((qkv, "qkv"), (q_norm_w, "q_norm_w"), (k_norm_w, "k_norm_w"), (q_out, "q_out")):
+        _f16_cuda(t, n)
+    num_pages, hkv, page_size = _pages(k_pages, v_pages, page_table)
+    _need(hkv == num_kv_heads, "k_pages head count mismatch")
+    hq = num_q_heads
+    B = qkv.shape[0] if qkv.dim() == 2 else 1
+    _need(qkv.numel() == B * (hq + 2 * hkv) * HEAD_DIM, f"qkv shape mismatch: {tuple(qkv.shape)}")
+    _need(q_out.numel() == B * hq * HEAD_DIM, f"q_out shape mismatch: {tuple(q_out.shape)}")
+    _need(position.is_cuda and position.dtype in (torch.int32, torch.uint32) and position.numel() >= B,
+          "position must be a device int32/uint32 tensor with one entry per sequence")
+    stride = page_table.shape[-1]
+    if max_seq is None:
+        max_seq = stride * page_size
+    dims = make_dims(hq, hkv, int(max_seq), eps)
+    _check(lib().grout_qk_norm_rope_kv_decode_paged(
+        _ptr(qkv), _ptr(q_norm_w), _ptr(k_norm_w), _ptr(rope_table), _ptr(q_out), _ptr(k_pages),
+        _ptr(v_pages), num_pages, page_size, _ptr(page_table), stride, _ptr(position), B,
+        ctypes.byref(dims), _stream(qkv)))
+    return q_out
+
+
+def qk_norm_rope_kv_prefill_paged(q, k, v, q_norm_w, k_norm_w, rope_table, q_out, k_pages, v_pages,
+                                  page_table_row, position_start, eps, max_seq=None):
+    """Fused prefill write of one sequence into a paged cache; page_table_row
+    is that sequence's row of the page table (device int32)."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v"), (q_norm_w, "q_norm_w"), (k_norm_w, "k_norm_w"),
+                 (q_out, "q_out")):
+        _f16_cuda(t, n)
+    num_pages, hkv, page_size = _pages(k_pages, v_pages, page_table_row)
+    _need(q.dim() == 3 and q.shape[2] == HEAD_DIM, f"q shape mismatch: {tuple(q.shape)}")
+    S, hq, _ = q.shape
+    _need(k.shape == (S, hkv, HEAD_DIM) and v.shape == k.shape, "k/v shape mismatch")
+    _need(q_out.shape == q.shape, "q_out shape mismatch")
+    if max_seq is None:
+        max_seq = page_table_row.numel() * page_size
+    _need(page_table_row.numel() * page_size >= max_seq, "page_table_row shorter than max_seq")
+    dims = make_dims(hq, hkv, int(max_seq), eps)
+    _check(lib().grout_qk_norm_rope_kv_prefill_paged(
+        _ptr(q), _ptr(k), _ptr(v), hq * HEAD_DIM, hkv * HEAD_DIM, _ptr(q_norm_w), _ptr(k_norm_w),
+        _ptr(rope_table), _ptr(q_out), _ptr(k_pages), _ptr(v_pages), num_pages, page_size,
+        _ptr(page_table_row), int(position_start), S, ctypes.byref(dims), _stream(q)))
+    return q_out
 
 
 def attention_decode_noalloc(q, k_cache, v_cache, position, out, max_kv_len, qk_scale=None,

@@ -533,4 +533,187 @@ grout_status grout_attn_decode(const void* q, const void* k_cache, const void* v
                               workspace_bytes, stream);
 }
 
+/* ----------------------------------------------------------- paged caches */
+
+static grout_status check_pages(const void* k_pages, const void* v_pages, int32_t num_pages,
+                                int32_t page_size, const int32_t* page_table,
+                                int64_t table_stride, const grout_attn_dims* dims) {
+  if (!k_pages || !v_pages || !page_table) return fail(GROUT_ERR_INVALID_ARG, "null pointer argument");
+  if (!aligned16(k_pages) || !aligned16(v_pages))
+    return fail(GROUT_ERR_INVALID_ARG, "page pools must be 16-byte aligned");
+  if (page_size < 64 || page_size > 4096 || page_size % 64)
+    return fail(GROUT_ERR_INVALID_ARG, "page_size=%d must be a multiple of 64 in [64, 4096]",
+                page_size);
+  if (num_pages < 1) return fail(GROUT_ERR_INVALID_ARG, "num_pages=%d", num_pages);
+  const int64_t need = ((int64_t)dims->max_seq + page_size - 1) / page_size;
+  if (table_stride < need)
+    return fail(GROUT_ERR_INVALID_ARG, "table_stride=%lld < ceil(max_seq / page_size)=%lld",
+                (long long)table_stride, (long long)need);
+  return GROUT_OK;
+}
+
+grout_status grout_attn_decode_paged(const void* q, const void* k_pages, const void* v_pages,
+                                     int32_t num_pages, int32_t page_size,
+                                     const int32_t* page_table, int32_t table_stride,
+                                     const uint32_t* d_position, void* out, int32_t batch,
+                                     int32_t max_kv_len, int32_t num_splits,
+                                     const grout_attn_dims* dims, void* workspace,
+                                     size_t workspace_bytes, grout_stream_t stream) {
+  grout_status st = check_dims(dims, 8);
+  if (st != GROUT_OK) return st;
+  if (batch < 0) return fail(GROUT_ERR_INVALID_ARG, "batch=%d", batch);
+  if (batch == 0) return GROUT_OK;  // empty call: nothing to read or write
+  if (!q || !out || !d_position) return fail(GROUT_ERR_INVALID_ARG, "null pointer argument");
+  if (!aligned16(q) || !aligned16(out))
+    return fail(GROUT_ERR_INVALID_ARG, "q and out must be 16-byte aligned");
+  st = check_pages(k_pages, v_pages, num_pages, page_size, page_table, table_stride, dims);
+  if (st != GROUT_OK) return st;
+  if (max_kv_len <= 0 || max_kv_len > dims->max_seq)
+    return fail(GROUT_ERR_INVALID_ARG, "max_kv_len=%d must be in [1, max_seq=%d]", max_kv_len,
+                dims->max_seq);
+  if (num_splits == 0) num_splits = grout_attn_decode_splits(batch, max_kv_len, dims);
+  if (num_splits < 1 || num_splits > 1024)
+    return fail(GROUT_ERR_INVALID_ARG, "num_splits=%d", num_splits);
+  const size_t need = decode_ws_bytes(batch, dims->num_q_heads, num_splits);
+  if (need > 0 && (!workspace || workspace_bytes < need || !aligned16(workspace)))
+    return fail(GROUT_ERR_INVALID_ARG, "workspace of %zu bytes (16-byte aligned) required, got %zu",
+                need, workspace ? workspace_bytes : (size_t)0);
+  DeviceState* ds;
+  st = current_state(&ds);
+  if (st != GROUT_OK) return st;
+  CUtensorMap tk, tv;
+  const uint64_t dk[4] = {128, (uint64_t)page_size, (uint64_t)dims->num_kv_heads,
+                          (uint64_t)num_pages};
+  const uint64_t sk[3] = {128, (uint64_t)page_size * 128,
+                          (uint64_t)page_size * 128 * (uint64_t)dims->num_kv_heads};
+  const uint32_t bk[4] = {64, 64, 1, 1};
+  st = encode_map(&tk, k_pages, 4, dk, sk, bk, "k_pages");
+  if (st != GROUT_OK) return st;
+  st = encode_map(&tv, v_pages, 4, dk, sk, bk, "v_pages");
+  if (st != GROUT_OK) return st;
+  DecodeArgs a{};
+  a.q = static_cast<const __half*>(q);
+  a.out = static_cast<__half*>(out);
+  a.part_o = static_cast<float*>(workspace);
+  a.part_lse = need ? static_cast<float*>(workspace) + (size_t)batch * dims->num_q_heads * num_splits * 128
+                    : nullptr;
+  a.d_position = d_position;
+  a.batch = batch;
+  a.hq = dims->num_q_heads;
+  a.hkv = dims->num_kv_heads;
+  a.nks = num_splits;
+  float scale = qk_scale(dims);
+  if (dims->flags & GROUT_FLAG_DECODE_SCALE_F16) scale = __half2float(__float2half_rn(scale));
+  a.scale_log2 = scale / logf(2.0f);
+  a.err = ds->err;
+  a.page_table = page_table;
+  a.table_stride = table_stride;
+  a.page_size = page_size;
+  a.num_pages = num_pages;
+  CUDA_TRY(launch_decode(a, tk, tv, reinterpret_cast<cudaStream_t>(stream)));
+  return GROUT_OK;
+}
+
+grout_status grout_qk_norm_rope_kv_decode_paged(
+    const void* qkv, const void* q_norm_w, const void* k_norm_w, const float* rope_table,
+    void* q_out, void* k_pages, void* v_pages, int32_t num_pages, int32_t page_size,
+    const int32_t* page_table, int32_t table_stride, const uint32_t* d_position, int32_t batch,
+    const grout_attn_dims* dims, grout_stream_t stream) {
+  grout_status st = check_dims(dims, 0);
+  if (st != GROUT_OK) return st;
+  if (batch < 0) return fail(GROUT_ERR_INVALID_ARG, "batch=%d", batch);
+  if (batch == 0) return GROUT_OK;
+  const void* ptrs[] = {qkv, q_norm_w, k_norm_w, rope_table, q_out};
+  for (const void* p : ptrs) {
+    if (!p) return fail(GROUT_ERR_INVALID_ARG, "null pointer argument");
+    if (!aligned16(p)) return fail(GROUT_ERR_INVALID_ARG, "pointer %p is not 16-byte aligned", p);
+  }
+  if (!d_position) return fail(GROUT_ERR_INVALID_ARG, "d_position is null");
+  st = check_pages(k_pages, v_pages, num_pages, page_size, page_table, table_stride, dims);
+  if (st != GROUT_OK) return st;
+  DeviceState* ds;
+  st = current_state(&ds);
+  if (st != GROUT_OK) return st;
+  NormRopeArgs a{};
+  a.q = static_cast<const __half*>(qkv);
+  a.q_row_stride = (int64_t)(dims->num_q_heads + 2 * dims->num_kv_heads) * 128;
+  a.q_w = static_cast<const __half*>(q_norm_w);
+  a.k_w = static_cast<const __half*>(k_norm_w);
+  a.table = rope_table;
+  a.q_out = static_cast<__half*>(q_out);
+  a.k_cache = static_cast<__half*>(k_pages);
+  a.v_cache = static_cast<__half*>(v_pages);
+  a.d_position = d_position;
+  a.rows = batch;
+  a.hq = dims->num_q_heads;
+  a.hkv = dims->num_kv_heads;
+  a.max_seq = dims->max_seq;
+  a.eps = dims->rms_eps;
+  a.decode = 1;
+  a.err = ds->err;
+  a.page_table = page_table;
+  a.table_stride = table_stride;
+  a.page_size = page_size;
+  a.num_pages = num_pages;
+  CUDA_TRY(launch_qk_norm_rope_kv(a, ds->num_sms, reinterpret_cast<cudaStream_t>(stream)));
+  return GROUT_OK;
+}
+
+grout_status grout_qk_norm_rope_kv_prefill_paged(
+    const void* q, const void* k, const void* v, int64_t q_row_stride, int64_t kv_row_stride,
+    const void* q_norm_w, const void* k_norm_w, const float* rope_table, void* q_out,
+    void* k_pages, void* v_pages, int32_t num_pages, int32_t page_size,
+    const int32_t* page_table, int32_t position_start, int32_t seq_len,
+    const grout_attn_dims* dims, grout_stream_t stream) {
+  grout_status st = check_dims(dims, 0);
+  if (st != GROUT_OK) return st;
+  if (seq_len == 0 && position_start >= 0 && position_start <= dims->max_seq) return GROUT_OK;
+  const void* ptrs[] = {q, k, v, q_norm_w, k_norm_w, rope_table, q_out};
+  for (const void* p : ptrs) {
+    if (!p) return fail(GROUT_ERR_INVALID_ARG, "null pointer argument");
+    if (!aligned16(p)) return fail(GROUT_ERR_INVALID_ARG, "pointer %p is not 16-byte aligned", p);
+  }
+  const int64_t table_len = ((int64_t)dims->max_seq + page_size - 1) / (page_size > 0 ? page_size : 1);
+  st = check_pages(k_pages, v_pages, num_pages, page_size, page_table, table_len, dims);
+  if (st != GROUT_OK) return st;
+  if (seq_len < 0 || position_start < 0)
+    return fail(GROUT_ERR_INVALID_ARG, "seq_len=%d position_start=%d", seq_len, position_start);
+  if ((int64_t)position_start + seq_len > dims->max_seq)
+    return fail(GROUT_ERR_INVALID_ARG, "fused qk/rope/kv range [%d..%lld) exceeds max_seq %d",
+                position_start, (long long)position_start + seq_len, dims->max_seq);
+  if (q_row_stride < (int64_t)dims->num_q_heads * 128 || q_row_stride % 8)
+    return fail(GROUT_ERR_INVALID_ARG, "q_row_stride=%lld", (long long)q_row_stride);
+  if (kv_row_stride < (int64_t)dims->num_kv_heads * 128 || kv_row_stride % 8)
+    return fail(GROUT_ERR_INVALID_ARG, "kv_row_stride=%lld", (long long)kv_row_stride);
+  DeviceState* ds;
+  st = current_state(&ds);
+  if (st != GROUT_OK) return st;
+  NormRopeArgs a{};
+  a.q = static_cast<const __half*>(q);
+  a.k = static_cast<const __half*>(k);
+  a.v = static_cast<const __half*>(v);
+  a.q_row_stride = q_row_stride;
+  a.kv_row_stride = kv_row_stride;
+  a.q_w = static_cast<const __half*>(q_norm_w);
+  a.k_w = static_cast<const __half*>(k_norm_w);
+  a.table = rope_table;
+  a.q_out = static_cast<__half*>(q_out);
+  a.k_cache = static_cast<__half*>(k_pages);
+  a.v_cache = static_cast<__half*>(v_pages);
+  a.pos0 = position_start;
+  a.rows = seq_len;
+  a.hq = dims->num_q_heads;
+  a.hkv = dims->num_kv_heads;
+  a.max_seq = dims->max_seq;
+  a.eps = dims->rms_eps;
+  a.decode = 0;
+  a.err = ds->err;
+  a.page_table = page_table;
+  a.table_stride = 0;
+  a.page_size = page_size;
+  a.num_pages = num_pages;
+  CUDA_TRY(launch_qk_norm_rope_kv(a, ds->num_sms, reinterpret_cast<cudaStream_t>(stream)));
+  return GROUT_OK;
+}
+
 }  // extern "C"

@@ -109,11 +109,20 @@ __global__ void __launch_bounds__(kThreads, 2)
         mbar_arrive_expect_tx(full, kStageBytes);
         const uint32_t kb = smem_u32(smem + st * kStageBytes);
         const uint32_t vb = kb + kTileBytes;
-        const int row = (t0 + it) * kKeys;
-        tma_load_4d(kb, &tm_k, full, 0, row, kh, b);
-        tma_load_4d(kb + kBoxBytes, &tm_k, full, 64, row, kh, b);
-        tma_load_4d(vb, &tm_v, full, 0, row, kh, b);
-        tma_load_4d(vb + kBoxBytes, &tm_v, full, 64, row, kh, b);
+        int row = (t0 + it) * kKeys;
+        int outer = b;  // sequence (contiguous caches) or page (paged pool)
+        if (a.page_table) {
+          // a 64-key tile never straddles a page (page_size % 64 == 0)
+          const int pg = row / a.page_size;
+          outer = __ldg(a.page_table + (int64_t)b * a.table_stride + pg);
+          row -= pg * a.page_size;
+          // an entry outside the pool reads the TMA fill (zeros): report it
+          if ((outer < 0 || outer >= a.num_pages) && a.err) atomicCAS(a.err, 0, DEV_ERR_PAGE);
+        }
+        tma_load_4d(kb, &tm_k, full, 0, row, kh, outer);
+        tma_load_4d(kb + kBoxBytes, &tm_k, full, 64, row, kh, outer);
+        tma_load_4d(vb, &tm_v, full, 0, row, kh, outer);
+        tma_load_4d(vb + kBoxBytes, &tm_v, full, 64, row, kh, outer);
       }
     }
   } else {

@@ -38,6 +38,14 @@ struct NormRopeArgs {
   float eps;
   int32_t decode;
   int* err;
+  // Paged cache (page_table != null): k_cache / v_cache are page pools
+  // [num_pages][hkv][page_size][128]; position p of sequence s is row
+  // p % page_size of page page_table[s * table_stride + p / page_size]
+  // (prefill: one sequence, table row page_table[0..]).
+  const int32_t* page_table;
+  int64_t table_stride;
+  int32_t page_size;
+  int32_t num_pages;
 };
 
 cudaError_t launch_qk_norm_rope_kv(const NormRopeArgs& a, int num_sms, cudaStream_t s);
@@ -54,6 +62,13 @@ struct DecodeArgs {
   int32_t nks;
   float scale_log2;
   int* err;
+  // Paged cache (page_table != null): the maps are {128, page_size, hkv,
+  // num_pages}; key row r of sequence b is row r % page_size of page
+  // page_table[b * table_stride + r / page_size].
+  const int32_t* page_table;
+  int32_t table_stride;
+  int32_t page_size;
+  int32_t num_pages;
 };
 
 // tm_k / tm_v: 4-D maps {128, max_seq, hkv, batch} over the caches, box

@@ -71,7 +71,16 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const NormRopeArgs
       if (is_q) {
         dst = a.q_out + ((int64_t)s * a.hq + hh) * kHeadDim;
       } else {
-        const int64_t off = (int64_t)s * a.cache_batch_stride + kh * a.cache_head_stride + pos * kHeadDim;
+        int64_t off = (int64_t)s * a.cache_batch_stride + kh * a.cache_head_stride + pos * kHeadDim;
+        if (a.page_table) {
+          const int64_t pg = pos / a.page_size;
+          const int32_t page = a.page_table[(int64_t)s * a.table_stride + pg];
+          if (page < 0 || page >= a.num_pages) {
+            if (j == 0 && a.err) atomicCAS(a.err, 0, DEV_ERR_PAGE);
+            continue;
+          }
+          off = ((int64_t)page * a.hkv + kh) * a.page_size * kHeadDim + (pos - pg * a.page_size) * kHeadDim;
+        }
         dst = a.k_cache + off;
         vdst = a.v_cache + off;
         vsrc = row + (int64_t)(a.hq + a.hkv + kh) * kHeadDim;
@@ -84,7 +93,16 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const NormRopeArgs
       } else {
         src = a.k + (int64_t)s * a.kv_row_stride + (int64_t)kh * kHeadDim;
         vsrc = a.v + (int64_t)s * a.kv_row_stride + (int64_t)kh * kHeadDim;
-        const int64_t off = kh * a.cache_head_stride + pos * kHeadDim;
+        int64_t off = kh * a.cache_head_stride + pos * kHeadDim;
+        if (a.page_table) {
+          const int64_t pg = pos / a.page_size;
+          const int32_t page = a.page_table[pg];
+          if (page < 0 || page >= a.num_pages) {
+            if (j == 0 && a.err) atomicCAS(a.err, 0, DEV_ERR_PAGE);
+            continue;
+          }
+          off = ((int64_t)page * a.hkv + kh) * a.page_size * kHeadDim + (pos - pg * a.page_size) * kHeadDim;
+        }
         dst = a.k_cache + off;
         vdst = a.v_cache + off;
       }

@@ -13,6 +13,7 @@ enum : int {
   DEV_ERR_NONE = 0,
   DEV_ERR_TIMEOUT_BASE = 0x100,  // + site id
   DEV_ERR_POSITION = 0x200,      // decode position >= max_seq
+  DEV_ERR_PAGE = 0x201,          // page-table entry outside [0, num_pages)
 };
 
 // A wait gives up after this many nanoseconds (globaltimer) and records a

@@ -274,6 +274,48 @@ grout_status grout_attn_decode_noalloc(const void* q, const void* k_cache, const
                                        int32_t max_kv_len, const grout_attn_dims* dims,
                                        grout_stream_t stream);
 
+/* ------------------------------------------------------ paged KV caches */
+
+/* Paged KV cache: no counterpart in the reference, whose caches are one
+ * contiguous [num_kv_heads][max_seq][128] tensor per layer
+ * (src/model.rs:1587-1599) and whose decode is batch-1 (src/kernels.rs:
+ * 4003-4004); the batched / paged cache is the serving extension next to it.
+ * Same math and rounding as the contiguous entry points.
+ *   k_pages, v_pages: page pools [num_pages][num_kv_heads][page_size][128] f16;
+ *   position p of sequence b lives in row p % page_size of page
+ *   page_table[b * table_stride + p / page_size] (int32, device);
+ *   page_size: a multiple of 64 in [64, 4096]; positions stay below
+ *   dims->max_seq and table_stride >= ceil(max_seq / page_size).
+ * A table entry outside [0, num_pages) is reported through
+ * grout_attn_check_device_error (0x201): the fused writes skip that row,
+ * decode reads zeros for that tile. */
+
+/* Paged form of grout_attn_decode_ex (num_splits 0 = the automatic count). */
+grout_status grout_attn_decode_paged(const void* q, const void* k_pages, const void* v_pages,
+                                     int32_t num_pages, int32_t page_size,
+                                     const int32_t* page_table, int32_t table_stride,
+                                     const uint32_t* d_position, void* out, int32_t batch,
+                                     int32_t max_kv_len, int32_t num_splits,
+                                     const grout_attn_dims* dims, void* workspace,
+                                     size_t workspace_bytes, grout_stream_t stream);
+
+/* Paged form of grout_qk_norm_rope_kv_decode: sequence b's new K/V row goes
+ * to position d_position[b]. */
+grout_status grout_qk_norm_rope_kv_decode_paged(
+    const void* qkv, const void* q_norm_w, const void* k_norm_w, const float* rope_table,
+    void* q_out, void* k_pages, void* v_pages, int32_t num_pages, int32_t page_size,
+    const int32_t* page_table, int32_t table_stride, const uint32_t* d_position, int32_t batch,
+    const grout_attn_dims* dims, grout_stream_t stream);
+
+/* Paged form of grout_qk_norm_rope_kv_prefill for one sequence: page_table is
+ * that sequence's row of the table (ceil(max_seq / page_size) entries). */
+grout_status grout_qk_norm_rope_kv_prefill_paged(
+    const void* q, const void* k, const void* v, int64_t q_row_stride, int64_t kv_row_stride,
+    const void* q_norm_w, const void* k_norm_w, const float* rope_table, void* q_out,
+    void* k_pages, void* v_pages, int32_t num_pages, int32_t page_size,
+    const int32_t* page_table, int32_t position_start, int32_t seq_len,
+    const grout_attn_dims* dims, grout_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -94,6 +94,30 @@ def test_validation_before_launch(L):
     assert st == 1 and "multiple" in _err(L)
 
 
+def test_paged_validation_before_launch(L):
+    """Paged entry points: page size, table stride, pool and table pointers
+    are checked on the host before any launch."""
+    p = ctypes.c_void_p(0x10000)
+    d = _dims()  # max_seq 4096
+    args = lambda ps, stride, pages=p, table=p: (p, pages, pages, 64, ps, table, stride, p, p, 2,
+                                                 100, 0, ctypes.byref(d), None, 0, None)
+    assert L.grout_attn_decode_paged(*args(96, 64)) == 1 and "page_size" in _err(L)
+    assert L.grout_attn_decode_paged(*args(32, 128)) == 1 and "page_size" in _err(L)
+    assert L.grout_attn_decode_paged(*args(64, 63)) == 1 and "table_stride" in _err(L)
+    assert L.grout_attn_decode_paged(*args(64, 64, table=None)) == 1 and "null" in _err(L)
+    assert L.grout_attn_decode_paged(*args(64, 64, pages=ctypes.c_void_p(0x10008))) == 1
+    assert "aligned" in _err(L)
+    st = L.grout_qk_norm_rope_kv_decode_paged(p, p, p, p, p, p, p, 0, 64, p, 64, p, 1,
+                                              ctypes.byref(d), None)
+    assert st == 1 and "num_pages" in _err(L)
+    st = L.grout_qk_norm_rope_kv_prefill_paged(p, p, p, 64 * 128, 8 * 128, p, p, p, p, p, p, 8,
+                                               128, p, 4000, 200, ctypes.byref(d), None)
+    assert st == 1 and "exceeds max_seq" in _err(L)
+    # empty batch: a no-op before any pointer check
+    assert L.grout_attn_decode_paged(None, None, None, 0, 0, None, 0, None, None, 0, 1, 0,
+                                     ctypes.byref(d), None, 0, None) == 0
+
+
 def test_init_without_gpu_fails_cleanly(L):
     import torch
     if torch.cuda.is_available():
