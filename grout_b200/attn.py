@@ -73,6 +73,25 @@ class PrefillVarlenArgs(ctypes.Structure):
     ]
 
 
+class PrefillPagedArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("q_row_stride", ctypes.c_int64),
+        ("q_rows", ctypes.c_int64),
+        ("k_pages", ctypes.c_void_p),
+        ("v_pages", ctypes.c_void_p),
+        ("num_pages", ctypes.c_int32),
+        ("page_size", ctypes.c_int32),
+        ("page_table", ctypes.c_void_p),
+        ("table_stride", ctypes.c_int32),
+        ("cu_seqlens_q", ctypes.c_void_p),
+        ("position_start", ctypes.c_void_p),
+        ("batch", ctypes.c_int32),
+        ("max_q_len", ctypes.c_int32),
+    ]
+
+
 # Every symbol include/grout_attn.h declares, with its ctypes signature.
 _vp, _i32, _i64, _f32, _sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
 _DIMS = ctypes.POINTER(AttnDims)
@@ -104,6 +123,7 @@ SIGNATURES = {
     "grout_attn_decode_noalloc_max_bytes": (_sz, []),
     "grout_attn_decode_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i32, _i32,
                                                  _DIMS, _vp]),
+    "grout_attn_prefill_paged": (ctypes.c_int, [ctypes.POINTER(PrefillPagedArgs), _DIMS, _vp]),
     "grout_attn_decode_paged": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _vp, _i32, _vp, _vp, _i32,
                                                _i32, _i32, _DIMS, _vp, _sz, _vp]),
     "grout_qk_norm_rope_kv_decode_paged": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32,
@@ -361,6 +381,39 @@ def _pages(k_pages, v_pages, page_table):
     _need(page_table.is_cuda and page_table.dtype == torch.int32 and page_table.is_contiguous(),
           "page_table must be a contiguous device int32 tensor")
     return k_pages.shape[0], k_pages.shape[1], k_pages.shape[2]
+
+
+def attention_prefill_paged(q, k_pages, v_pages, page_table, out, cu_seqlens_q=None,
+                            position_start=None, max_q_len=None, max_seq=None, qk_scale=None):
+    """Causal prefill over a paged cache.  q, out packed [q_rows, Hq, 128];
+    page pools [num_pages, Hkv, page_size, 128]; page_table [B, table_stride]
+    device int32; cu_seqlens_q device int32 [B+1] (None: one sequence of all
+    q rows); position_start device int32 [B] (None: all 0)."""
+    for t, n in ((q, "q"), (out, "out")):
+        _f16_cuda(t, n)
+    num_pages, hkv, page_size = _pages(k_pages, v_pages, page_table)
+    _need(out.shape == q.shape, "out shape mismatch")
+    hq = q.shape[1]
+    if cu_seqlens_q is not None:
+        _need(cu_seqlens_q.is_cuda and cu_seqlens_q.dtype == torch.int32, "cu_seqlens_q must be device int32")
+        B = cu_seqlens_q.numel() - 1
+        _need(max_q_len is not None, "max_q_len is required with cu_seqlens_q")
+    else:
+        B = 1
+        max_q_len = q.shape[0] if max_q_len is None else max_q_len
+    if position_start is not None:
+        _need(position_start.is_cuda and position_start.dtype == torch.int32, "position_start must be device int32")
+    stride = page_table.shape[-1]
+    if max_seq is None:
+        max_seq = stride * page_size
+    args = PrefillPagedArgs(
+        q.data_ptr(), out.data_ptr(), hq * HEAD_DIM, q.shape[0], k_pages.data_ptr(), v_pages.data_ptr(),
+        num_pages, page_size, page_table.data_ptr(), stride,
+        cu_seqlens_q.data_ptr() if cu_seqlens_q is not None else None,
+        position_start.data_ptr() if position_start is not None else None, B, int(max_q_len))
+    dims = make_dims(hq, hkv, int(max_seq), qk_scale=qk_scale)
+    _check(lib().grout_attn_prefill_paged(ctypes.byref(args), ctypes.byref(dims), _stream(q)))
+    return out
 
 
 def attention_decode_paged(q, k_pages, v_pages, page_table, position, out, max_kv_len,

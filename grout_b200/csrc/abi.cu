@@ -552,6 +552,69 @@ static grout_status check_pages(const void* k_pages, const void* v_pages, int32_
   return GROUT_OK;
 }
 
+grout_status grout_attn_prefill_paged(const grout_prefill_paged_args* p,
+                                      const grout_attn_dims* dims, grout_stream_t stream) {
+  if (!p) return fail(GROUT_ERR_INVALID_ARG, "args is null");
+  grout_status st = check_dims(dims, 0);
+  if (st != GROUT_OK) return st;
+  if (p->batch < 0 || p->max_q_len < 0)
+    return fail(GROUT_ERR_INVALID_ARG, "batch=%d max_q_len=%d", p->batch, p->max_q_len);
+  if (p->batch == 0 || p->max_q_len == 0) return GROUT_OK;
+  if (!p->q || !p->out) return fail(GROUT_ERR_INVALID_ARG, "null pointer argument");
+  if (!aligned16(p->q) || !aligned16(p->out))
+    return fail(GROUT_ERR_INVALID_ARG, "q and out must be 16-byte aligned");
+  if (!p->cu_seqlens_q && p->batch != 1)
+    return fail(GROUT_ERR_INVALID_ARG, "cu_seqlens_q is null with batch=%d", p->batch);
+  st = check_pages(p->k_pages, p->v_pages, p->num_pages, p->page_size, p->page_table,
+                   p->table_stride, dims);
+  if (st != GROUT_OK) return st;
+  const int64_t hq = dims->num_q_heads, hkv = dims->num_kv_heads;
+  if (p->q_row_stride < hq * 128 || p->q_row_stride % 8)
+    return fail(GROUT_ERR_INVALID_ARG, "q_row_stride=%lld", (long long)p->q_row_stride);
+  if (p->q_rows <= 0 || (!p->cu_seqlens_q && p->q_rows < p->max_q_len))
+    return fail(GROUT_ERR_INVALID_ARG, "q_rows=%lld", (long long)p->q_rows);
+  if (!p->position_start && p->max_q_len > dims->max_seq)
+    return fail(GROUT_ERR_INVALID_ARG, "max_q_len=%d exceeds max_seq %d", p->max_q_len,
+                dims->max_seq);
+  DeviceState* ds;
+  st = current_state(&ds);
+  if (st != GROUT_OK) return st;
+  CUtensorMap tq, tk, tv;
+  const uint64_t dq[3] = {128, (uint64_t)hq, (uint64_t)p->q_rows};
+  const uint64_t sq[2] = {128, (uint64_t)p->q_row_stride};
+  const uint32_t bq[3] = {64, 1, 128};
+  st = encode_map(&tq, p->q, 3, dq, sq, bq, "q");
+  if (st != GROUT_OK) return st;
+  const uint64_t dk[4] = {128, (uint64_t)p->page_size, (uint64_t)hkv, (uint64_t)p->num_pages};
+  const uint64_t sk[3] = {128, (uint64_t)p->page_size * 128, (uint64_t)p->page_size * 128 * hkv};
+  const uint32_t bk[4] = {64, 64, 1, 1};
+  st = encode_map(&tk, p->k_pages, 4, dk, sk, bk, "k_pages");
+  if (st != GROUT_OK) return st;
+  st = encode_map(&tv, p->v_pages, 4, dk, sk, bk, "v_pages");
+  if (st != GROUT_OK) return st;
+  PrefillArgs a{};
+  a.out = static_cast<__half*>(p->out);
+  a.q_row_stride = p->q_row_stride;
+  a.cu_q = p->cu_seqlens_q;
+  a.pos0 = p->position_start;
+  a.kv_start = nullptr;
+  a.batch = p->batch;
+  a.max_q_len = p->max_q_len;
+  a.hq = (int32_t)hq;
+  a.hkv = (int32_t)hkv;
+  a.kv_batched = 0;
+  a.single_len = p->max_q_len;
+  a.single_pos0 = 0;
+  a.scale_log2 = qk_scale(dims) / logf(2.0f);
+  a.err = ds->err;
+  a.page_table = p->page_table;
+  a.table_stride = p->table_stride;
+  a.page_size = p->page_size;
+  a.num_pages = p->num_pages;
+  CUDA_TRY(launch_prefill(a, tq, tk, tv, reinterpret_cast<cudaStream_t>(stream)));
+  return GROUT_OK;
+}
+
 grout_status grout_attn_decode_paged(const void* q, const void* k_pages, const void* v_pages,
                                      int32_t num_pages, int32_t page_size,
                                      const int32_t* page_table, int32_t table_stride,

@@ -92,6 +92,13 @@ struct PrefillArgs {
   int32_t single_pos0;       // used when pos0 == null
   float scale_log2;
   int* err;
+  // Paged K/V (page_table != null): the K/V maps are {128, page_size, hkv,
+  // num_pages} with 64-row boxes; key n of sequence b is row n % page_size of
+  // page page_table[b * table_stride + n / page_size].
+  const int32_t* page_table;
+  int32_t table_stride;
+  int32_t page_size;
+  int32_t num_pages;
 };
 
 // tm_q: 3-D {128, hq, q_rows}, box {64, 1, 128}; tm_k / tm_v: 4-D

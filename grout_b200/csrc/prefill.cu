@@ -279,7 +279,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           const CUtensorMap* map = (i & 1) ? &tm_v : &tm_k;
           const uint32_t dst = smem_base + kOffKV + slot * kTile;
           const int row = it.ks + (i >> 1) * kBN;
-          if (a.kv_batched) {
+          if (a.page_table) {
+            // two 64-key halves, each inside one page (page_size % 64 == 0);
+            // a half past the sequence's last key reads page 0 (masked) and
+            // leaves the table untouched
+            const int32_t* trow = a.page_table + (int64_t)it.b * a.table_stride;
+            const int kv_len = it.P + it.S;
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const int key = (i >> 1) * kBN + hh * 64;
+              int page = 0, r = 0;
+              if (key < kv_len) {
+                const int pg = key / a.page_size;
+                page = __ldg(trow + pg);
+                r = key - pg * a.page_size;
+                if ((page < 0 || page >= a.num_pages) && a.err) atomicCAS(a.err, 0, DEV_ERR_PAGE);
+              }
+              tma_load_4d(dst + hh * (kBox / 2), map, full, 0, r, kh, page);
+              tma_load_4d(dst + kBox + hh * (kBox / 2), map, full, 64, r, kh, page);
+            }
+          } else if (a.kv_batched) {
             tma_load_4d(dst, map, full, 0, row, kh, kvb);
             tma_load_4d(dst + kBox, map, full, 64, row, kh, kvb);
           } else {

@@ -290,6 +290,36 @@ grout_status grout_attn_decode_noalloc(const void* q, const void* k_cache, const
  * grout_attn_check_device_error (0x201): the fused writes skip that row,
  * decode reads zeros for that tile. */
 
+/* Causal prefill attention over a paged cache (chunked prefill: the chunk's
+ * K/V were written with grout_qk_norm_rope_kv_prefill_paged).  Same math as
+ * grout_attn_prefill_varlen.
+ *   q, out: packed [q_rows][num_q_heads][128], row stride q_row_stride;
+ *     sequence b owns rows cu_seqlens_q[b] .. cu_seqlens_q[b+1] (DEVICE
+ *     int32 [batch+1]; NULL with batch 1 = rows 0 .. max_q_len);
+ *   position_start[b] (DEVICE int32 [batch], NULL = all 0): keys of
+ *     sequence b are positions 0 .. position_start[b] + len_b - 1 of its
+ *     pages, row m sees keys <= position_start[b] + m;
+ *   max_q_len: host upper bound on any len_b. */
+typedef struct {
+  const void* q;
+  void* out;
+  int64_t q_row_stride;
+  int64_t q_rows;
+  const void* k_pages;
+  const void* v_pages;
+  int32_t num_pages;
+  int32_t page_size;
+  const int32_t* page_table;
+  int32_t table_stride;
+  const int32_t* cu_seqlens_q;
+  const int32_t* position_start;
+  int32_t batch;
+  int32_t max_q_len;
+} grout_prefill_paged_args;
+
+grout_status grout_attn_prefill_paged(const grout_prefill_paged_args* args,
+                                      const grout_attn_dims* dims, grout_stream_t stream);
+
 /* Paged form of grout_attn_decode_ex (num_splits 0 = the automatic count). */
 grout_status grout_attn_decode_paged(const void* q, const void* k_pages, const void* v_pages,
                                      int32_t num_pages, int32_t page_size,

@@ -151,3 +151,52 @@ def test_bad_page_entry_is_reported_without_a_write(grout):
     with pytest.raises(grout.GroutError, match="0x201"):
         grout.check_device_error()
     grout.check_device_error()  # cleared
+
+
+@pytest.mark.parametrize("page_size", [64, 128, 192])
+def test_paged_prefill_single_sequence_bitwise_equals_contiguous(grout, page_size):
+    """Chunked prefill at a position offset: the same cache in shuffled pages
+    gives the contiguous kernel's bits (tiles straddling pages included)."""
+    S, hq, hkv, pos0 = 500, 64, 8, 300
+    ms = 1152  # a multiple of 64, 128 and 192
+    dev = torch.device("cuda", 0)
+    q = torch.from_numpy(synth.normal(80, S * hq * D).reshape(S, hq, D)).to(dev)
+    kc = torch.from_numpy(synth.normal(81, hkv * ms * D).reshape(hkv, ms, D)).to(dev)
+    vc = torch.from_numpy(synth.normal(82, hkv * ms * D).reshape(hkv, ms, D)).to(dev)
+    ref = torch.empty_like(q)
+    grout.attention_prefill(q, kc, vc, ref, pos0)
+    kp, table = _paged(kc[None], page_size, 5)
+    vp, _ = _paged(vc[None], page_size, 5)
+    out = torch.empty_like(q)
+    grout.attention_prefill_paged(q, kp, vp, table, out,
+                                  position_start=torch.tensor([pos0], dtype=torch.int32, device=dev))
+    torch.cuda.synchronize()
+    grout.check_device_error()
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+
+
+def test_paged_prefill_varlen_bitwise_equals_batched_cache(grout):
+    """Ragged batch with per-sequence position offsets over one shared pool."""
+    hq, hkv, ms, ps = 16, 4, 1024, 128
+    lens = np.array([200, 77, 513], np.int32)
+    pos0 = np.array([0, 300, 500], np.int32)
+    B = len(lens)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    tot = int(cu[-1])
+    dev = torch.device("cuda", 0)
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    q = T(synth.normal(91, tot * hq * D).reshape(tot, hq, D))
+    kc = T(synth.normal(92, B * hkv * ms * D).reshape(B, hkv, ms, D))
+    vc = T(synth.normal(93, B * hkv * ms * D).reshape(B, hkv, ms, D))
+    ref = torch.zeros(tot, hq, D, dtype=torch.float16, device=dev)
+    grout.attention_prefill_varlen(q, kc, vc, ref, T(cu), int(lens.max()), hkv, kv_row_stride=D,
+                                   kv_head_stride=ms * D, kv_batch_stride=hkv * ms * D, kv_rows=ms,
+                                   position_start=T(pos0))
+    kp, table = _paged(kc, ps, 6)
+    vp, _ = _paged(vc, ps, 6)
+    out = torch.zeros_like(ref)
+    grout.attention_prefill_paged(q, kp, vp, table, out, cu_seqlens_q=T(cu), position_start=T(pos0),
+                                  max_q_len=int(lens.max()))
+    torch.cuda.synchronize()
+    grout.check_device_error()
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
