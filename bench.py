@@ -369,6 +369,7 @@ def run_ours(args, rank, world, local_rank):
         line["e2e_decode_c5"] = c5
     if world == 1 and not args.no_decode:
         line["decode"] = decode_grid(args, dev, pk)
+        line["decode_paged"] = decode_paged_cells(args, dev, pk)
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline()
     return line
@@ -498,6 +499,49 @@ def decode_grid(args, dev, pk):
     big = [c for c in cells if c["B"] * c["L"] >= 8 * 8192]
     return {"unit": "GB/s", "peak_gbs": pk["hbm_gbs"], "cells": cells,
             "mean_frac_large_cells": round(statistics.mean(c["frac"] for c in big), 4)}
+
+
+def decode_paged_cells(args, dev, pk):
+    """The paged KV cache (page-pool layout [num_pages, Hkv, page_size, D],
+    pages of each sequence shuffled across the pool) on config-3 cells, timed
+    like decode_grid; bytes per cell are the same as the contiguous cell's."""
+    import torch
+    import grout_b200 as g
+    flush = L2Flush(dev)
+    reps = max(3, min(args.steps, 10))
+    cells = []
+    for B, L, ps in ((8, 8192, 64), (32, 16384, 128), (64, 32768, 256)):
+        hq, hkv = 64, 8
+        per = L // ps
+        n = B * per
+        gen = torch.Generator().manual_seed(7)
+        table = torch.randperm(n, generator=gen).view(B, per).to(torch.int32).to(dev)
+        kp = torch.randn(n, hkv, ps, D, device=dev, dtype=torch.float16)
+        vp = torch.randn_like(kp)
+        q = torch.randn(B, hq, D, device=dev, dtype=torch.float16)
+        out = torch.empty_like(q)
+        pos = torch.full((B,), L - 1, dtype=torch.int32, device=dev)
+        ws = torch.empty(max(16, g.decode_workspace_bytes(B, L, hq, hkv, L)), dtype=torch.uint8, device=dev)
+        graph = capture(lambda: g.attention_decode_paged(q, kp, vp, table, pos, out, L, workspace=ws))
+        ts = []
+        for _ in range(reps):
+            flush()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        us = statistics.median(ts) * 1e3
+        nbytes = B * (2 * hkv * L * D * 2 + 2 * hq * D * 2)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        cells.append({"B": B, "L": L, "page_size": ps, "us": round(us, 2), "gbs": round(gbs, 1),
+                      "frac": round(gbs / pk["hbm_gbs"], 4)})
+        del kp, vp
+        torch.cuda.empty_cache()
+    g.check_device_error()
+    return {"unit": "GB/s", "layout": "page pool [num_pages, Hkv, page_size, 128], shuffled pages",
+            "cells": cells}
 
 
 # ------------------------------------------------------------ reference arm
