@@ -370,6 +370,7 @@ def run_ours(args, rank, world, local_rank):
     if world == 1 and not args.no_decode:
         line["decode"] = decode_grid(args, dev, pk)
         line["decode_paged"] = decode_paged_cells(args, dev, pk)
+        line["prefill_splitk"] = prefill_splitk_cell(args, dev, pk)
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline()
     return line
@@ -501,6 +502,43 @@ def decode_grid(args, dev, pk):
             "mean_frac_large_cells": round(statistics.mean(c["frac"] for c in big), 4)}
 
 
+def prefill_splitk_cell(args, dev, pk):
+    """A launch with fewer work items than SMs (one sequence, S = 2048, 8/1
+    heads: 64 items for 148 SMs) with and without the split-K path."""
+    import ctypes
+    import torch
+    import grout_b200 as g
+    flush = L2Flush(dev)
+    S, hq, hkv = 2048, 8, 1
+    q = torch.randn(S, hq, D, device=dev, dtype=torch.float16)
+    k = torch.randn(hkv, S, D, device=dev, dtype=torch.float16)
+    v = torch.randn_like(k)
+    out = torch.empty_like(q)
+    flops = 4.0 * D * hq * S * (S + 1) / 2
+    nks = g.lib().grout_attn_prefill_splits(1, S, ctypes.byref(g.attn.make_dims(hq, hkv, S)))
+    ws = torch.empty(max(16, g.lib().grout_attn_prefill_splitk_workspace_bytes(1, S, hq, nks)),
+                     dtype=torch.uint8, device=dev)
+    res = {"workload": "one sequence, S=2048, 8 query / 1 KV heads (64 items)", "splits": nks}
+    for name, fn in (("unsplit", lambda: g.attention_prefill(q, k, v, out, 0)),
+                     ("split", lambda: g.attention_prefill_splitk(
+                         q, k, v, out, None, S, hkv, kv_row_stride=D, kv_head_stride=S * D,
+                         kv_rows=S, num_splits=nks, workspace=ws))):
+        graph = capture(fn)
+        ts = []
+        for _ in range(max(3, min(args.steps, 10))):
+            flush()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        us = statistics.median(ts) * 1e3
+        res[name] = {"us": round(us, 2), "tflops": round(flops / (us * 1e-6) / 1e12, 1)}
+    g.check_device_error()
+    return res
+
+
 def decode_paged_cells(args, dev, pk):
     """The paged KV cache (page-pool layout [num_pages, Hkv, page_size, D],
     pages of each sequence shuffled across the pool) on config-3 cells, timed
@@ -626,7 +664,12 @@ def main():
         dev = torch.device("cuda", local_rank)
         torch.cuda.set_device(dev)
         g.init(local_rank)
-        line = {"decode": decode_grid(args, dev, peaks())} if rank == 0 else None
+        if rank == 0:
+            pk = peaks()
+            line = {"decode": decode_grid(args, dev, pk), "decode_paged": decode_paged_cells(args, dev, pk),
+                    "prefill_splitk": prefill_splitk_cell(args, dev, pk)}
+        else:
+            line = None
     else:
         line = run_ours(args, rank, world, local_rank)
     if line is not None:

@@ -11,6 +11,7 @@ from .attn import (  # noqa: F401
     attention_decode_paged,
     attention_prefill,
     attention_prefill_paged,
+    attention_prefill_splitk,
     attention_prefill_varlen,
     check_device_error,
     decode_splits,

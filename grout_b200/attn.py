@@ -123,6 +123,10 @@ SIGNATURES = {
     "grout_attn_decode_noalloc_max_bytes": (_sz, []),
     "grout_attn_decode_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i32, _i32,
                                                  _DIMS, _vp]),
+    "grout_attn_prefill_splits": (_i32, [_i32, _i32, _DIMS]),
+    "grout_attn_prefill_splitk_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32]),
+    "grout_attn_prefill_splitk": (ctypes.c_int, [ctypes.POINTER(PrefillVarlenArgs), _i32, _DIMS, _vp,
+                                                 _sz, _vp]),
     "grout_attn_prefill_paged": (ctypes.c_int, [ctypes.POINTER(PrefillPagedArgs), _DIMS, _vp]),
     "grout_attn_decode_paged": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _vp, _i32, _vp, _vp, _i32,
                                                _i32, _i32, _DIMS, _vp, _sz, _vp]),
@@ -324,6 +328,42 @@ def attention_prefill_varlen(q, k, v, out, cu_seqlens_q, max_q_len, num_kv_heads
         kv_start.data_ptr() if kv_start is not None else None, B, int(max_q_len))
     dims = make_dims((hi - lo) * G, hi - lo, 1 << 30, qk_scale=qk_scale)
     _check(lib().grout_attn_prefill_varlen(ctypes.byref(args), ctypes.byref(dims), _stream(q)))
+    return out
+
+
+def attention_prefill_splitk(q, k, v, out, cu_seqlens_q, max_q_len, num_kv_heads,
+                             kv_row_stride, kv_head_stride, kv_batch_stride=0, kv_rows=None,
+                             position_start=None, kv_start=None, num_splits=None, workspace=None,
+                             qk_scale=None):
+    """Split-K form of attention_prefill_varlen for launches with fewer work
+    items than SMs (same arguments; cu_seqlens_q may be None for one
+    sequence of q.shape[0] rows).  num_splits None = the library's choice."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v"), (out, "out")):
+        _f16_cuda(t, n)
+    _need(out.shape == q.shape, "out shape mismatch")
+    hq = q.shape[1]
+    if cu_seqlens_q is not None:
+        _need(cu_seqlens_q.is_cuda and cu_seqlens_q.dtype == torch.int32, "cu_seqlens_q must be device int32")
+        B = cu_seqlens_q.numel() - 1
+    else:
+        B = 1
+    if kv_rows is None:
+        kv_rows = (k.numel() - (B - 1) * kv_batch_stride) // max(1, kv_row_stride) if kv_batch_stride else k.numel() // kv_row_stride
+    dims = make_dims(hq, num_kv_heads, 1 << 30, qk_scale=qk_scale)
+    if num_splits is None:
+        num_splits = lib().grout_attn_prefill_splits(B, int(max_q_len), ctypes.byref(dims))
+    need = lib().grout_attn_prefill_splitk_workspace_bytes(B, int(max_q_len), hq, int(num_splits))
+    if need and workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    args = PrefillVarlenArgs(
+        q.data_ptr(), out.data_ptr(), hq * HEAD_DIM, q.shape[0], k.data_ptr(), v.data_ptr(),
+        kv_batch_stride, kv_row_stride, kv_head_stride, int(kv_rows),
+        cu_seqlens_q.data_ptr() if cu_seqlens_q is not None else None,
+        position_start.data_ptr() if position_start is not None else None,
+        kv_start.data_ptr() if kv_start is not None else None, B, int(max_q_len))
+    _check(lib().grout_attn_prefill_splitk(ctypes.byref(args), int(num_splits), ctypes.byref(dims),
+                                           _ptr(workspace), ws_bytes, _stream(q)))
     return out
 
 

@@ -5,6 +5,7 @@
 // execute_qk_norm_rope_kv_prefill_op_ctx (src/model.rs:4771-4822) and
 // attend_seq_arc_into_ctx_with_position (src/model.rs:6864-6937): every
 // shape/range problem is reported before any device work.
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -336,7 +337,8 @@ grout_status grout_qk_norm_rope_kv_decode(const void* qkv, const void* q_norm_w,
 
 static grout_status prefill_common(const grout_prefill_varlen_args* p, int32_t single_len,
                                    int32_t single_pos0, const grout_attn_dims* dims,
-                                   grout_stream_t stream) {
+                                   grout_stream_t stream, int32_t nsplit = 1,
+                                   void* workspace = nullptr, size_t workspace_bytes = 0) {
   grout_status st = check_dims(dims, 0);
   if (st != GROUT_OK) return st;
   if (p->batch == 0 || p->max_q_len == 0) return GROUT_OK;
@@ -397,8 +399,52 @@ static grout_status prefill_common(const grout_prefill_varlen_args* p, int32_t s
   a.single_pos0 = single_pos0;
   a.scale_log2 = qk_scale(dims) / logf(2.0f);
   a.err = ds->err;
+  a.nsplit = nsplit;
+  if (nsplit > 1) {
+    const size_t need = grout_attn_prefill_splitk_workspace_bytes(p->batch, p->max_q_len,
+                                                                  (int32_t)hq, nsplit);
+    if (!workspace || workspace_bytes < need || !aligned16(workspace))
+      return fail(GROUT_ERR_INVALID_ARG, "workspace of %zu bytes (16-byte aligned) required, got %zu",
+                  need, workspace ? workspace_bytes : (size_t)0);
+    a.part = static_cast<float*>(workspace);
+  }
   CUDA_TRY(launch_prefill(a, tq, tk, tv, reinterpret_cast<cudaStream_t>(stream)));
   return GROUT_OK;
+}
+
+int32_t grout_attn_prefill_splits(int32_t batch, int32_t max_q_len, const grout_attn_dims* dims) {
+  if (!dims || batch <= 0 || max_q_len <= 0 || dims->num_q_heads <= 0) return 1;
+  DeviceState* ds;
+  int sms = 148;
+  if (current_state(&ds) == GROUT_OK) sms = ds->num_sms;
+  const int64_t items = (int64_t)((max_q_len + 255) / 256) * dims->num_q_heads * batch;
+  if (items >= sms) return 1;
+  // enough items to cover the SMs, and chunks of at least four KV tiles
+  int32_t n = (int32_t)((sms + items - 1) / items);
+  const int32_t tiles = (max_q_len + 127) / 128;
+  n = std::min(n, std::max(1, tiles / 4));
+  return std::max(1, std::min(n, 8));
+}
+
+size_t grout_attn_prefill_splitk_workspace_bytes(int32_t batch, int32_t max_q_len,
+                                                 int32_t num_q_heads, int32_t num_splits) {
+  if (batch <= 0 || max_q_len <= 0 || num_q_heads <= 0 || num_splits <= 1) return 0;
+  const size_t base_items = (size_t)((max_q_len + 255) / 256) * num_q_heads * batch;
+  return base_items * num_splits * 2 * kPrefillPartFloats * sizeof(float);
+}
+
+grout_status grout_attn_prefill_splitk(const grout_prefill_varlen_args* args, int32_t num_splits,
+                                       const grout_attn_dims* dims, void* workspace,
+                                       size_t workspace_bytes, grout_stream_t stream) {
+  if (!args) return fail(GROUT_ERR_INVALID_ARG, "args is null");
+  if (num_splits < 1 || num_splits > 8)
+    return fail(GROUT_ERR_INVALID_ARG, "num_splits=%d must be in [1, 8]", num_splits);
+  if (!args->cu_seqlens_q && args->batch != 1)
+    return fail(GROUT_ERR_INVALID_ARG, "cu_seqlens_q is null with batch=%d", args->batch);
+  // position_start is per sequence on the device; single sequences without
+  // cu_seqlens use position 0 (pass position_start for an offset)
+  return prefill_common(args, args->cu_seqlens_q ? 0 : args->max_q_len, 0, dims, stream,
+                        num_splits, workspace, workspace_bytes);
 }
 
 grout_status grout_attn_prefill(const void* q, const void* k_cache, const void* v_cache,
@@ -611,6 +657,7 @@ grout_status grout_attn_prefill_paged(const grout_prefill_paged_args* p,
   a.table_stride = p->table_stride;
   a.page_size = p->page_size;
   a.num_pages = p->num_pages;
+  a.nsplit = 1;
   CUDA_TRY(launch_prefill(a, tq, tk, tv, reinterpret_cast<cudaStream_t>(stream)));
   return GROUT_OK;
 }

@@ -99,11 +99,18 @@ struct PrefillArgs {
   int32_t table_stride;
   int32_t page_size;
   int32_t num_pages;
+  // Split-K (nsplit > 1): every (pair, head, sequence) item is cut into
+  // nsplit KV ranges; each writes its unnormalised O and (m, l) per row to
+  // part ([item][tile][128 rows][130] f32) and a merge kernel finishes.
+  int32_t nsplit;
+  float* part;
 };
 
 // tm_q: 3-D {128, hq, q_rows}, box {64, 1, 128}; tm_k / tm_v: 4-D
 // {128, kv_rows, hkv, B} (or 3-D without the batch dim), box {64, 128, 1(,1)};
 // all 128B swizzle.
+// Number of f32 in one split partial of one query tile: O[128][128], m[128], l[128].
+constexpr int kPrefillPartFloats = 128 * 130;
 cudaError_t launch_prefill(const PrefillArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                            const CUtensorMap& tm_v, cudaStream_t s);
 cudaError_t prefill_set_attributes();

@@ -55,8 +55,8 @@ constexpr int kRegsSoftmax = 192;
 constexpr int kOffQ = 0;                       // 2 query tiles
 constexpr int kOffKV = 2 * kTile;              // ring
 constexpr int kOffBar = kOffKV + kSlots * kTile;
-constexpr int kOffL = kOffBar + 512;           // row sums [item parity][tile][row]
-constexpr int kSmemBytes = kOffL + 2 * 2 * 128 * 4 + 1024;
+constexpr int kOffL = kOffBar + 512;           // row sums, then row maxima: [2][item parity][tile][row]
+constexpr int kSmemBytes = kOffL + 2 * 2 * 2 * 128 * 4 + 1024;
 
 // barrier indices (phases run on across the work items of a CTA)
 constexpr int kBarQ = 0;                      // + tile: Q_t landed (TMA)
@@ -167,8 +167,16 @@ __device__ __forceinline__ void mma_ts_lo(uint32_t d, uint32_t a_tmem, uint32_t 
 // the causal work per CTA (a plain stride leaves the first CTAs ~12% more).
 struct Item {
   int h, b, q0, S, P, ks, q_start, n_kv, n_kv0;
+  int lo;   // first KV tile of this item (split-K: its range starts here)
+  int nch;  // split-K: number of non-empty splits of this (pair, head, sequence)
 };
+template <bool kSplit>
 __device__ __forceinline__ bool decode_item(const PrefillArgs& a, int idx, int n_pairs, Item& it) {
+  int split = 0;
+  if (kSplit) {
+    split = idx % a.nsplit;
+    idx /= a.nsplit;
+  }
   const int per = a.hq * a.batch;
   const int pair = n_pairs - 1 - idx / per;
   const int rem = idx - (idx / per) * per;
@@ -189,9 +197,26 @@ __device__ __forceinline__ bool decode_item(const PrefillArgs& a, int idx, int n
   it.n_kv = (it.P + rows_hi + kBN - 1) / kBN;
   // query tile 0 (rows q0 .. q0+127) never sees keys beyond P + q0 + 127
   it.n_kv0 = (it.P + min(it.q0 + kBM, it.S) + kBN - 1) / kBN;
+  it.lo = 0;
+  it.nch = 1;
+  if (kSplit) {
+    // Split [0, n_kv0) into chunks of tps tiles; the last chunk also takes
+    // tile 1's extra tile, so both tiles have work in every chunk.
+    const int tps = (it.n_kv0 + a.nsplit - 1) / a.nsplit;
+    it.nch = (it.n_kv0 + tps - 1) / tps;
+    const int lo = split * tps;
+    if (lo >= it.n_kv0) return false;  // fewer chunks than splits
+    const int hi0 = min(it.n_kv0, lo + tps);
+    it.lo = lo;
+    it.n_kv = hi0 == it.n_kv0 ? it.n_kv - lo : hi0 - lo;
+    it.n_kv0 = hi0 - lo;
+  }
   return true;
 }
 
+// kPaged: K/V from a page pool; kSplit: split-K partial output.  The plain
+// instantiation carries neither.
+template <bool kPaged, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
@@ -206,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int n_pairs = (a.max_q_len + 2 * kBM - 1) / (2 * kBM);
-  const int n_items = n_pairs * a.hq * a.batch;
+  const int n_items = n_pairs * a.hq * a.batch * (kSplit ? a.nsplit : 1);
   auto item_of = [&](int r) {
     return r * (int)gridDim.x + ((r & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x);
   };
@@ -244,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int r = 0, idx; ok && (idx = item_of(r)) < n_items; ++r) {
         Item it;
-        if (!decode_item(a, idx, n_pairs, it)) continue;
+        if (!decode_item<kSplit>(a, idx, n_pairs, it)) continue;
         const int kh = it.h / (a.hq / a.hkv);
         const int kvb = a.kv_batched ? it.b : 0;
         // Q_0, K_0, Q_1, then the rest: each tile's query buffer is refilled
@@ -278,8 +303,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(full, kTile);
           const CUtensorMap* map = (i & 1) ? &tm_v : &tm_k;
           const uint32_t dst = smem_base + kOffKV + slot * kTile;
-          const int row = it.ks + (i >> 1) * kBN;
-          if (a.page_table) {
+          const int row = it.ks + (it.lo + (i >> 1)) * kBN;
+          if (kPaged) {
             // two 64-key halves, each inside one page (page_size % 64 == 0);
             // a half past the sequence's last key reads page 0 (masked) and
             // leaves the table untouched
@@ -287,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int kv_len = it.P + it.S;
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-              const int key = (i >> 1) * kBN + hh * 64;
+              const int key = (it.lo + (i >> 1)) * kBN + hh * 64;
               int page = 0, r = 0;
               if (key < kv_len) {
                 const int pg = key / a.page_size;
@@ -342,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // half-period offset across item boundaries.
     auto next_valid = [&](int& rr, Item& itm) -> bool {
       for (int idx; (idx = item_of(rr)) < n_items; ++rr)
-        if (decode_item(a, idx, n_pairs, itm)) return true;
+        if (decode_item<kSplit>(a, idx, n_pairs, itm)) return true;
       return false;
     };
     int ring = 0, nq = 0, pc0 = 0, pc1 = 0;
@@ -454,16 +479,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int r = 0, idx; ok && (idx = item_of(r)) < n_items; ++r) {
       Item it;
-      if (!decode_item(a, idx, n_pairs, it)) continue;
+      if (!decode_item<kSplit>(a, idx, n_pairs, it)) continue;
 #pragma unroll 1
       for (int t = 0; t < 2; ++t) {
         ok = mbar_wait(smem_u32(&bars[kBarOfull + t]), nq & 1, a.err, 40 + t, abort_flag);
         ok = ok && mbar_wait(smem_u32(&bars[kBarL + t]), nq & 1, a.err, 42 + t, abort_flag);
         if (!ok) break;
         tc_fence_after();
-        const float inv_l = 1.0f / fmaxf(lbuf[((nq & 1) * 2 + t) * 128 + row], 1.0e-8f);
+        const float l_row = lbuf[((nq & 1) * 2 + t) * 128 + row];
+        const float inv_l = 1.0f / fmaxf(l_row, 1.0e-8f);
         const int row_q = it.q0 + t * kBM + row;
         const bool valid = row_q < it.S;
+        // split-K: this item's unnormalised rows and (m, l) go to the workspace
+        float* prow = kSplit ? a.part + ((size_t)idx * 2 + t) * kPrefillPartFloats : nullptr;
+        if (prow && valid) {
+          prow[128 * 128 + row] = lbuf[512 + ((nq & 1) * 2 + t) * 128 + row];
+          prow[128 * 129 + row] = l_row;
+        }
         __half* orow = a.out + (int64_t)(it.q_start + row_q) * a.q_row_stride + (int64_t)it.h * 128;
         const uint32_t tO = tmem + 256 + t * 128 + lane_off;
 #pragma unroll 1
@@ -476,7 +508,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&bars[kBarOempty + t]));
           }
-          if (valid) {
+          if (prow && valid) {
+            float4* dst = reinterpret_cast<float4*>(prow + row * 128 + c * 32);
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                   __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+          } else if (valid) {
             uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
@@ -506,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int r = 0, idx; ok && (idx = item_of(r)) < n_items; ++r) {
       Item it;
-      if (!decode_item(a, idx, n_pairs, it)) continue;
+      if (!decode_item<kSplit>(a, idx, n_pairs, it)) continue;
       const int row_q = it.q0 + t * kBM + row;
       const int kv_len = it.P + it.S;
       const int key_lim = min(it.P + row_q, kv_len - 1);  // last visible key
@@ -526,7 +564,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 4; ++c)
   #pragma unroll
           for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[c][i]);
-        const int lim = key_lim - j * kBN;
+        const int lim = key_lim - (it.lo + j) * kBN;
         if (lim < kBN - 1) {
   #pragma unroll
           for (int c = 0; c < 128; ++c)
@@ -610,6 +648,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
       }
       lbuf[((nq & 1) * 2 + t) * 128 + row] = l;
+      lbuf[512 + ((nq & 1) * 2 + t) * 128 + row] = m_run;
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bars[kBarL + t]));
       ++nq;
@@ -624,17 +663,92 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Split-K merge (prefill_splitk_reduce_merge, src/kernels.rs:3302-3759):
+// per query row, M = max_s m_s, w_s = 2^(m_s - M),
+// out = sum_s w_s O_s / max(sum_s w_s l_s, 1e-8), rounded to f16.
+// One CTA per (item, query tile), decoded once; warp w takes rows w, w+32,
+// w+64, w+96 and lane l dimensions 4l..4l+3, every split's loads issued
+// together (the split loop is unrolled to kMaxSplits).
+constexpr int kMaxSplits = 8;
+__global__ void __launch_bounds__(1024) prefill_merge_kernel(const PrefillArgs a) {
+  __shared__ int s_nch, s_rows;
+  __shared__ int64_t s_out_row, s_h;
+  const int t = blockIdx.x & 1;
+  const int base = blockIdx.x >> 1;  // item index without the split
+  if (threadIdx.x == 0) {
+    const int n_pairs = (a.max_q_len + 2 * kBM - 1) / (2 * kBM);
+    Item it;
+    int nch = 0;
+    if (decode_item<true>(a, base * a.nsplit, n_pairs, it)) {
+      nch = it.nch;
+      s_rows = min(kBM, it.S - (it.q0 + t * kBM));
+      s_out_row = it.q_start + it.q0 + t * kBM;
+      s_h = it.h;
+    }
+    s_nch = nch;
+  }
+  __syncthreads();
+  const int nch = s_nch;
+  if (nch == 0 || s_rows <= 0) return;  // empty item (ragged batch) or tile
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* p0 = a.part + ((size_t)base * a.nsplit * 2 + t) * kPrefillPartFloats;
+  const size_t sstride = (size_t)2 * kPrefillPartFloats;  // next split, same item and tile
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = warp + 32 * i;
+    if (r >= s_rows) break;
+    float m[kMaxSplits], l[kMaxSplits];
+    float4 o[kMaxSplits];
+#pragma unroll
+    for (int sp = 0; sp < kMaxSplits; ++sp) {
+      if (sp < nch) {
+        const float* ps = p0 + sp * sstride;
+        m[sp] = ps[128 * 128 + r];
+        l[sp] = ps[128 * 129 + r];
+        o[sp] = reinterpret_cast<const float4*>(ps + r * 128)[lane];
+      }
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int sp = 0; sp < kMaxSplits; ++sp)
+      if (sp < nch) M = fmaxf(M, m[sp]);
+    float W = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int sp = 0; sp < kMaxSplits; ++sp) {
+      if (sp < nch) {
+        const float w = ex2(m[sp] - M);
+        W += w * l[sp];
+        acc.x += w * o[sp].x;
+        acc.y += w * o[sp].y;
+        acc.z += w * o[sp].z;
+        acc.w += w * o[sp].w;
+      }
+    }
+    const float inv = 1.0f / fmaxf(W, 1.0e-8f);
+    uint2 u;
+    u.x = pack_half2(acc.x * inv, acc.y * inv);
+    u.y = pack_half2(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<uint2*>(a.out + (s_out_row + r) * a.q_row_stride + s_h * 128 + 4 * lane) = u;
+  }
+}
+
 }  // namespace
 
 cudaError_t prefill_set_attributes() {
-  return cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              kSmemBytes);
+  for (auto k : {prefill_kernel<false, false>, prefill_kernel<true, false>,
+                 prefill_kernel<false, true>, prefill_kernel<true, true>}) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 cudaError_t launch_prefill(const PrefillArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                            const CUtensorMap& tm_v, cudaStream_t s) {
   const int n_pairs = (a.max_q_len + 2 * kBM - 1) / (2 * kBM);
-  const long long n_items = (long long)n_pairs * a.hq * a.batch;
+  if (a.nsplit < 1 || a.nsplit > kMaxSplits || (a.nsplit > 1 && !a.part)) return cudaErrorInvalidValue;
+  const long long n_items = (long long)n_pairs * a.hq * a.batch * a.nsplit;
   if (n_items == 0) return cudaSuccess;
   static int num_sms[64] = {0};
   int dev = 0;
@@ -645,7 +759,18 @@ cudaError_t launch_prefill(const PrefillArgs& a, const CUtensorMap& tm_q, const 
     if (e != cudaSuccess) return e;
   }
   const int grid = (int)(n_items < num_sms[dev] ? n_items : num_sms[dev]);
-  prefill_kernel<<<grid, kThreads, kSmemBytes, s>>>(tm_q, tm_k, tm_v, a);
+  const bool paged = a.page_table != nullptr, split = a.nsplit > 1;
+  if (paged && split)
+    prefill_kernel<true, true><<<grid, kThreads, kSmemBytes, s>>>(tm_q, tm_k, tm_v, a);
+  else if (paged)
+    prefill_kernel<true, false><<<grid, kThreads, kSmemBytes, s>>>(tm_q, tm_k, tm_v, a);
+  else if (split)
+    prefill_kernel<false, true><<<grid, kThreads, kSmemBytes, s>>>(tm_q, tm_k, tm_v, a);
+  else
+    prefill_kernel<false, false><<<grid, kThreads, kSmemBytes, s>>>(tm_q, tm_k, tm_v, a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || a.nsplit <= 1) return e;
+  prefill_merge_kernel<<<(unsigned)(n_items / a.nsplit * 2), 1024, 0, s>>>(a);
   return cudaGetLastError();
 }
 

@@ -177,6 +177,22 @@ typedef struct {
 grout_status grout_attn_prefill_varlen(const grout_prefill_varlen_args* args,
                                        const grout_attn_dims* dims, grout_stream_t stream);
 
+/* Split-K varlen prefill: the reference's prefill split-K + merge
+ * (fmha_prefill_gqa_lpt_split / prefill_splitk_reduce_merge,
+ * src/kernels.rs:3302-3759, microbench only there).  For launches with fewer
+ * (query-tile pair, head, sequence) items than SMs: every item's KV range is
+ * cut into num_splits chunks, each writes its unnormalised rows and (max,
+ * sum) to the workspace, and a merge rounds the combined rows to f16.
+ * Same arguments as grout_attn_prefill_varlen (cu_seqlens_q may be NULL for
+ * batch 1); results agree with it within the usual tolerance, not bitwise.
+ * grout_attn_prefill_splits suggests a count (1 = no split needed). */
+int32_t grout_attn_prefill_splits(int32_t batch, int32_t max_q_len, const grout_attn_dims* dims);
+size_t grout_attn_prefill_splitk_workspace_bytes(int32_t batch, int32_t max_q_len,
+                                                 int32_t num_q_heads, int32_t num_splits);
+grout_status grout_attn_prefill_splitk(const grout_prefill_varlen_args* args, int32_t num_splits,
+                                       const grout_attn_dims* dims, void* workspace,
+                                       size_t workspace_bytes, grout_stream_t stream);
+
 /* --------------------------------------------------------- decode attention */
 
 /* Number of KV splits grout_attn_decode uses for this shape (a function of

@@ -118,6 +118,17 @@ def test_paged_validation_before_launch(L):
                                      ctypes.byref(d), None, 0, None) == 0
 
 
+def test_prefill_split_heuristic(L):
+    """Split-K prefill only for launches with fewer work items than SMs."""
+    d = _dims(hq=64, hkv=8)
+    assert L.grout_attn_prefill_splits(1, 4096, ctypes.byref(d)) == 1   # 1024 items
+    d = _dims(hq=8, hkv=1)
+    n = L.grout_attn_prefill_splits(1, 2048, ctypes.byref(d))         # 64 items
+    assert 2 <= n <= 8
+    assert L.grout_attn_prefill_splitk_workspace_bytes(1, 2048, 8, 1) == 0
+    assert L.grout_attn_prefill_splitk_workspace_bytes(1, 2048, 8, 3) == 8 * 8 * 3 * 2 * 128 * 130 * 4
+
+
 def test_init_without_gpu_fails_cleanly(L):
     import torch
     if torch.cuda.is_available():
