@@ -200,3 +200,61 @@ def test_paged_prefill_varlen_bitwise_equals_batched_cache(grout):
     torch.cuda.synchronize()
     grout.check_device_error()
     assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+
+
+def test_paged_decode_graph_replay_across_pages(grout):
+    """A decode step (fused paged write + paged attention) recorded once in a
+    CUDA graph and replayed while positions grow across a page boundary; the
+    next page is appended to the table between steps (outside the graph).
+    Every step equals the contiguous-cache path bit for bit."""
+    B, hq, hkv, ms, ps = 2, 32, 8, 512, 64
+    eps, theta = 1e-6, 1.0e6
+    dev = torch.device("cuda", 0)
+    qw = torch.from_numpy(synth.norm_weight(4, D)).to(dev)
+    kw = torch.from_numpy(synth.norm_weight(5, D)).to(dev)
+    table = grout.rope_table(theta, ms, dev)
+    # contiguous reference caches and a paged pool holding the same rows
+    kc = torch.from_numpy(synth.normal(141, B * hkv * ms * D).reshape(B, hkv, ms, D)).to(dev)
+    vc = torch.from_numpy(synth.normal(142, B * hkv * ms * D).reshape(B, hkv, ms, D)).to(dev)
+    kp, ptab = _paged(kc, ps, 9)
+    vp, _ = _paged(vc, ps, 9)
+    live = ptab.clone()
+    ptab[:, 1:] = -1  # pages past the first are appended as positions grow
+    qkv = torch.empty(B, (hq + 2 * hkv) * D, dtype=torch.float16, device=dev)
+    pos = torch.zeros(B, dtype=torch.int32, device=dev)
+    q_out = torch.empty(B, hq, D, dtype=torch.float16, device=dev)
+    out = torch.empty_like(q_out)
+    ws = torch.empty(max(16, grout.decode_workspace_bytes(B, ms, hq, hkv, ms)), dtype=torch.uint8, device=dev)
+
+    def step():
+        grout.qk_norm_rope_kv_decode_paged(qkv, qw, kw, table, q_out, kp, vp, ptab, pos, hq, hkv, eps)
+        grout.attention_decode_paged(q_out, kp, vp, ptab, pos, out, ms, workspace=ws)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        qkv.copy_(torch.randn_like(qkv))
+        pos.fill_(0)
+        step()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            step()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    grout.check_device_error()
+    q_ref = torch.empty_like(q_out)
+    o_ref = torch.empty_like(out)
+    # the warm-up step wrote position 0 into the pool: mirror it
+    grout.qk_norm_rope_kv_decode(qkv, qw, kw, table, q_ref, kc, vc, pos, hq, hkv, eps)
+    for p in (60, 62, 63, 64, 65, 127, 128):
+        pg = p // ps
+        ptab[:, pg] = live[:, pg]  # the page this position lands in
+        qkv.copy_(torch.from_numpy(synth.normal(150 + p, qkv.numel()).reshape(qkv.shape)).to(dev))
+        pos.fill_(p)
+        g.replay()
+        grout.qk_norm_rope_kv_decode(qkv, qw, kw, table, q_ref, kc, vc, pos, hq, hkv, eps)
+        grout.attention_decode(q_ref, kc, vc, pos, o_ref, ms)
+        torch.cuda.synchronize()
+        grout.check_device_error()
+        assert torch.equal(q_out.view(torch.int16), q_ref.view(torch.int16)), p
+        assert torch.equal(out.view(torch.int16), o_ref.view(torch.int16)), p
