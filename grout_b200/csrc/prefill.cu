@@ -556,23 +556,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++sc;
         tc_fence_after();
         uint32_t r[4][32];
-  #pragma unroll
+#pragma unroll
         for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, r[c]);
         tc_wait_ld();
         float s[128];
-  #pragma unroll
+#pragma unroll
         for (int c = 0; c < 4; ++c)
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[c][i]);
         const int lim = key_lim - (it.lo + j) * kBN;
         if (lim < kBN - 1) {
-  #pragma unroll
+#pragma unroll
           for (int c = 0; c < 128; ++c)
             if (c > lim) s[c] = -INFINITY;
         }
         float mx0 = fmaxf(s[0], s[1]), mx1 = fmaxf(s[2], s[3]);
         float mx2 = fmaxf(s[4], s[5]), mx3 = fmaxf(s[6], s[7]);
-  #pragma unroll
+#pragma unroll
         for (int c = 8; c < 128; c += 8) {
           mx0 = fmax3(mx0, s[c], s[c + 1]);
           mx1 = fmax3(mx1, s[c + 2], s[c + 3]);
@@ -590,10 +590,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t sl2x2 = f2pack(sl2, sl2);
         const uint64_t negm2 = f2pack(-m_use, -m_use);
         uint64_t rsum = f2pack(0.f, 0.f);
-  #pragma unroll
+#pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < 16; ++i) {
             const uint64_t x2 = ffma2(f2pack(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1]), sl2x2, negm2);
             float p0, p1;
@@ -623,12 +623,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // (PV_t(j-1) has completed: it was issued before the QK that produced
         // this S).
         if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-  #pragma unroll 1
+#pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
             tmem_ld32(tO + c * 32, o);
             tc_wait_ld();
-  #pragma unroll
+#pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
             tmem_st32(tO + c * 32, o);
           }
