@@ -23,6 +23,7 @@ from .attn import (  # noqa: F401
     qk_norm_rope_kv_decode_paged,
     qk_norm_rope_kv_prefill,
     qk_norm_rope_kv_prefill_paged,
+    qkv_proj_norm_rope_kv_prefill,
     rope_table,
 )
 

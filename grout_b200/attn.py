@@ -123,6 +123,9 @@ SIGNATURES = {
     "grout_attn_decode_noalloc_max_bytes": (_sz, []),
     "grout_attn_decode_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i32, _i32,
                                                  _DIMS, _vp]),
+    "grout_qkv_proj_norm_rope_kv_prefill": (ctypes.c_int, [_vp, _i64, _vp, _i32, _vp, _vp, _vp, _vp,
+                                                           _vp, _vp, _i64, _vp, _i32, _i32, _DIMS,
+                                                           _vp]),
     "grout_attn_prefill_splits": (_i32, [_i32, _i32, _DIMS]),
     "grout_attn_prefill_splitk_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32]),
     "grout_attn_prefill_splitk": (ctypes.c_int, [ctypes.POINTER(PrefillVarlenArgs), _i32, _DIMS, _vp,
@@ -329,6 +332,34 @@ def attention_prefill_varlen(q, k, v, out, cu_seqlens_q, max_q_len, num_kv_heads
     dims = make_dims((hi - lo) * G, hi - lo, 1 << 30, qk_scale=qk_scale)
     _check(lib().grout_attn_prefill_varlen(ctypes.byref(args), ctypes.byref(dims), _stream(q)))
     return out
+
+
+def qkv_proj_norm_rope_kv_prefill(x, w_qkv, q_norm_w, k_norm_w, rope_table, q_out, k_cache,
+                                  v_cache, position_start, eps, qkv_out=None):
+    """QKV projection of a prefill chunk with the fused norm/RoPE/KV write
+    as its epilogue: x [S, hidden]; w_qkv [(Hq+2Hkv)*128, hidden] (torch
+    Linear layout); q_out [S, Hq, 128]; caches [Hkv, max_seq, 128];
+    qkv_out (optional) [S, (Hq+2Hkv)*128] receives the f16 projection."""
+    for t, n in ((x, "x"), (w_qkv, "w_qkv"), (q_norm_w, "q_norm_w"), (k_norm_w, "k_norm_w"),
+                 (q_out, "q_out"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        _f16_cuda(t, n)
+    _need(x.dim() == 2 and x.stride(1) == 1, "x must be [S, hidden] with unit column stride")
+    S, hidden = x.shape
+    hkv, max_seq = k_cache.shape[0], k_cache.shape[1]
+    hq = q_out.shape[1]
+    _need(q_out.shape == (S, hq, HEAD_DIM), f"q_out shape mismatch: {tuple(q_out.shape)}")
+    _need(w_qkv.shape == ((hq + 2 * hkv) * HEAD_DIM, hidden) and w_qkv.is_contiguous(),
+          f"w_qkv must be [{(hq + 2 * hkv) * HEAD_DIM}, {hidden}] contiguous")
+    _need(v_cache.shape == k_cache.shape, "v_cache shape mismatch")
+    if qkv_out is not None:
+        _f16_cuda(qkv_out, "qkv_out")
+        _need(qkv_out.shape == (S, (hq + 2 * hkv) * HEAD_DIM) and qkv_out.is_contiguous(), "qkv_out shape mismatch")
+    dims = make_dims(hq, hkv, max_seq, eps)
+    _check(lib().grout_qkv_proj_norm_rope_kv_prefill(
+        _ptr(x), x.stride(0), _ptr(w_qkv), hidden, _ptr(q_norm_w), _ptr(k_norm_w), _ptr(rope_table),
+        _ptr(q_out), _ptr(k_cache), _ptr(v_cache), max_seq * HEAD_DIM, _ptr(qkv_out),
+        int(position_start), S, ctypes.byref(dims), _stream(x)))
+    return q_out
 
 
 def attention_prefill_splitk(q, k, v, out, cu_seqlens_q, max_q_len, num_kv_heads,

@@ -177,6 +177,7 @@ grout_status grout_attn_init(int32_t device) {
   }
   CUDA_TRY(decode_set_attributes());
   CUDA_TRY(prefill_set_attributes());
+  CUDA_TRY(qkv_gemm_set_attributes());
   void* err = nullptr;
   CUDA_TRY(cudaGetSymbolAddress(&err, g_device_error));
   CUDA_TRY(cudaMemset(err, 0, sizeof(int)));
@@ -823,6 +824,71 @@ grout_status grout_qk_norm_rope_kv_prefill_paged(
   a.page_size = page_size;
   a.num_pages = num_pages;
   CUDA_TRY(launch_qk_norm_rope_kv(a, ds->num_sms, reinterpret_cast<cudaStream_t>(stream)));
+  return GROUT_OK;
+}
+
+grout_status grout_qkv_proj_norm_rope_kv_prefill(
+    const void* x, int64_t x_row_stride, const void* w_qkv, int32_t hidden, const void* q_norm_w,
+    const void* k_norm_w, const float* rope_table, void* q_out, void* k_cache, void* v_cache,
+    int64_t cache_head_stride, void* qkv_out, int32_t position_start, int32_t seq_len,
+    const grout_attn_dims* dims, grout_stream_t stream) {
+  grout_status st = check_dims(dims, 0);
+  if (st != GROUT_OK) return st;
+  if (seq_len == 0 && position_start >= 0 && position_start <= dims->max_seq) return GROUT_OK;
+  const void* ptrs[] = {x, w_qkv, q_norm_w, k_norm_w, rope_table, q_out, k_cache, v_cache};
+  for (const void* p : ptrs) {
+    if (!p) return fail(GROUT_ERR_INVALID_ARG, "null pointer argument");
+    if (!aligned16(p)) return fail(GROUT_ERR_INVALID_ARG, "pointer %p is not 16-byte aligned", p);
+  }
+  if (qkv_out && !aligned16(qkv_out))
+    return fail(GROUT_ERR_INVALID_ARG, "qkv_out is not 16-byte aligned");
+  if (seq_len < 0 || position_start < 0)
+    return fail(GROUT_ERR_INVALID_ARG, "seq_len=%d position_start=%d", seq_len, position_start);
+  if ((int64_t)position_start + seq_len > dims->max_seq)
+    return fail(GROUT_ERR_INVALID_ARG, "fused qkv/rope/kv range [%d..%lld) exceeds max_seq %d",
+                position_start, (long long)position_start + seq_len, dims->max_seq);
+  if (hidden <= 0 || hidden % 64)
+    return fail(GROUT_ERR_INVALID_ARG, "hidden=%d must be a positive multiple of 64", hidden);
+  if (x_row_stride < hidden || x_row_stride % 8)
+    return fail(GROUT_ERR_INVALID_ARG, "x_row_stride=%lld", (long long)x_row_stride);
+  if (cache_head_stride < (int64_t)dims->max_seq * 128 || cache_head_stride % 8)
+    return fail(GROUT_ERR_INVALID_ARG, "cache_head_stride=%lld", (long long)cache_head_stride);
+  DeviceState* ds;
+  st = current_state(&ds);
+  if (st != GROUT_OK) return st;
+  const int64_t heads = (int64_t)dims->num_q_heads + 2 * dims->num_kv_heads;
+  CUtensorMap tx, tw;
+  {
+    const uint64_t dx[3] = {(uint64_t)hidden, (uint64_t)seq_len, 1};
+    const uint64_t sx[2] = {(uint64_t)x_row_stride, (uint64_t)x_row_stride * (uint64_t)seq_len};
+    const uint32_t bx[3] = {64, 128, 1};
+    st = encode_map(&tx, x, 3, dx, sx, bx, "x");
+    if (st != GROUT_OK) return st;
+    const uint64_t dw[3] = {(uint64_t)hidden, (uint64_t)(heads * 128), 1};
+    const uint64_t sw[2] = {(uint64_t)hidden, (uint64_t)hidden * (uint64_t)(heads * 128)};
+    const uint32_t bw[3] = {64, 256, 1};  // one tile's 256 output features
+    st = encode_map(&tw, w_qkv, 3, dw, sw, bw, "w_qkv");
+    if (st != GROUT_OK) return st;
+  }
+  QkvGemmArgs a{};
+  a.rows = seq_len;
+  a.hidden = hidden;
+  a.hq = dims->num_q_heads;
+  a.hkv = dims->num_kv_heads;
+  a.pos0 = position_start;
+  a.eps = dims->rms_eps;
+  a.q_w = static_cast<const __half*>(q_norm_w);
+  a.k_w = static_cast<const __half*>(k_norm_w);
+  a.table = rope_table;
+  a.q_out = static_cast<__half*>(q_out);
+  a.q_out_row_stride = (int64_t)dims->num_q_heads * 128;
+  a.k_cache = static_cast<__half*>(k_cache);
+  a.v_cache = static_cast<__half*>(v_cache);
+  a.cache_head_stride = cache_head_stride;
+  a.qkv_out = static_cast<__half*>(qkv_out);
+  a.qkv_row_stride = heads * 128;
+  a.err = ds->err;
+  CUDA_TRY(launch_qkv_gemm(a, tx, tw, ds->num_sms, reinterpret_cast<cudaStream_t>(stream)));
   return GROUT_OK;
 }
 

@@ -115,4 +115,30 @@ cudaError_t launch_prefill(const PrefillArgs& a, const CUtensorMap& tm_q, const 
                            const CUtensorMap& tm_v, cudaStream_t s);
 cudaError_t prefill_set_attributes();
 
+// QKV projection + fused norm/RoPE/KV write (prefill): X [rows][hidden] f16
+// (row stride x_row_stride) times W [(hq+2hkv)*128][hidden] f16; maps are
+// 3-D {hidden, rows or features, 1} with 64x128 boxes, 128B swizzle.
+struct QkvGemmArgs {
+  int32_t rows;
+  int32_t hidden;
+  int32_t hq;
+  int32_t hkv;
+  int32_t pos0;
+  float eps;
+  const __half* q_w;
+  const __half* k_w;
+  const float* table;
+  __half* q_out;
+  int64_t q_out_row_stride;
+  __half* k_cache;
+  __half* v_cache;
+  int64_t cache_head_stride;
+  __half* qkv_out;           // optional f16 QKV activation
+  int64_t qkv_row_stride;
+  int* err;
+};
+cudaError_t launch_qkv_gemm(const QkvGemmArgs& a, const CUtensorMap& tm_x, const CUtensorMap& tm_w,
+                            int num_sms, cudaStream_t s);
+cudaError_t qkv_gemm_set_attributes();
+
 }  // namespace grout

@@ -290,6 +290,23 @@ grout_status grout_attn_decode_noalloc(const void* q, const void* k_cache, const
                                        int32_t max_kv_len, const grout_attn_dims* dims,
                                        grout_stream_t stream);
 
+/* QKV projection with the fused norm/RoPE/KV write as its epilogue
+ * (prefill): replaces the QKV MatMulSlice (src/model.rs:4076-4098) plus
+ * grout_qk_norm_rope_kv_prefill, without the f16 QKV activation round trip.
+ *   x [seq_len][hidden] f16 (row stride x_row_stride), hidden % 64 == 0;
+ *   w_qkv [(num_q_heads + 2*num_kv_heads)*128][hidden] f16 (torch Linear
+ *     layout: Q heads, then K heads, then V heads);
+ *   outputs as grout_qk_norm_rope_kv_prefill (q_out [seq_len][num_q_heads][128]);
+ *   qkv_out (nullable): [seq_len][(num_q_heads + 2*num_kv_heads)*128] f16, the
+ *     projection itself.
+ * The accumulators are rounded to f16 before the norm, so q_out and the
+ * caches equal grout_qk_norm_rope_kv_prefill applied to qkv_out bit for bit. */
+grout_status grout_qkv_proj_norm_rope_kv_prefill(
+    const void* x, int64_t x_row_stride, const void* w_qkv, int32_t hidden, const void* q_norm_w,
+    const void* k_norm_w, const float* rope_table, void* q_out, void* k_cache, void* v_cache,
+    int64_t cache_head_stride, void* qkv_out, int32_t position_start, int32_t seq_len,
+    const grout_attn_dims* dims, grout_stream_t stream);
+
 /* ------------------------------------------------------ paged KV caches */
 
 /* Paged KV cache: no counterpart in the reference, whose caches are one
