@@ -371,6 +371,7 @@ def run_ours(args, rank, world, local_rank):
         line["decode"] = decode_grid(args, dev, pk)
         line["decode_paged"] = decode_paged_cells(args, dev, pk)
         line["prefill_splitk"] = prefill_splitk_cell(args, dev, pk)
+        line["qkv_proj_epilogue"] = qkv_proj_cell(args, dev, pk)
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline()
     return line
@@ -539,6 +540,51 @@ def prefill_splitk_cell(args, dev, pk):
     return res
 
 
+def qkv_proj_cell(args, dev, pk):
+    """Config 2's QKV projection (S = 4096, hidden 5120 -> 80 heads x 128)
+    with the fused norm/RoPE/KV write as its epilogue, against the unfused
+    pair it replaces (cuBLAS GEMM into an f16 activation + the fused kernel)."""
+    import torch
+    import grout_b200 as g
+    flush = L2Flush(dev)
+    S, hidden, hq, hkv = 4096, 5120, 64, 8
+    N = (hq + 2 * hkv) * D
+    x = torch.randn(S, hidden, device=dev, dtype=torch.float16)
+    w = (torch.randn(N, hidden, device=dev) * 0.02).half()
+    ones = torch.ones(D, dtype=torch.float16, device=dev)
+    table = g.rope_table(1.0e6, S, dev)
+    q_out = torch.empty(S, hq, D, dtype=torch.float16, device=dev)
+    kc = torch.zeros(hkv, S, D, dtype=torch.float16, device=dev)
+    vc = torch.zeros_like(kc)
+    qkv = torch.empty(S, N, dtype=torch.float16, device=dev)
+    qv = qkv.view(S, hq + 2 * hkv, D)
+
+    def unfused():
+        torch.matmul(x, w.t(), out=qkv)
+        g.qk_norm_rope_kv_prefill(qv[:, :hq], qv[:, hq:hq + hkv], qv[:, hq + hkv:], ones, ones, table,
+                                  q_out, kc, vc, 0, 1e-6)
+
+    flops = 2.0 * S * hidden * N
+    res = {"workload": "QKV projection S=4096, 5120 -> 10240, + norm/RoPE/KV write", "gemm_flops": flops}
+    for name, fn in (("fused_epilogue", lambda: g.qkv_proj_norm_rope_kv_prefill(
+                         x, w, ones, ones, table, q_out, kc, vc, 0, 1e-6)),
+                     ("cublas_gemm_plus_fused_kernel", unfused)):
+        graph = capture(fn)
+        ts = []
+        for _ in range(max(3, min(args.steps, 10))):
+            flush()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        us = statistics.median(ts) * 1e3
+        res[name] = {"us": round(us, 2), "tflops": round(flops / (us * 1e-6) / 1e12, 1)}
+    g.check_device_error()
+    return res
+
+
 def decode_paged_cells(args, dev, pk):
     """The paged KV cache (page-pool layout [num_pages, Hkv, page_size, D],
     pages of each sequence shuffled across the pool) on config-3 cells, timed
@@ -667,7 +713,8 @@ def main():
         if rank == 0:
             pk = peaks()
             line = {"decode": decode_grid(args, dev, pk), "decode_paged": decode_paged_cells(args, dev, pk),
-                    "prefill_splitk": prefill_splitk_cell(args, dev, pk)}
+                    "prefill_splitk": prefill_splitk_cell(args, dev, pk),
+                    "qkv_proj_epilogue": qkv_proj_cell(args, dev, pk)}
         else:
             line = None
     else:
