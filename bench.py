@@ -544,6 +544,7 @@ def qkv_proj_cell(args, dev, pk):
     """Config 2's QKV projection (S = 4096, hidden 5120 -> 80 heads x 128)
     with the fused norm/RoPE/KV write as its epilogue, against the unfused
     pair it replaces (cuBLAS GEMM into an f16 activation + the fused kernel)."""
+    import ctypes
     import torch
     import grout_b200 as g
     flush = L2Flush(dev)
@@ -557,12 +558,21 @@ def qkv_proj_cell(args, dev, pk):
     kc = torch.zeros(hkv, S, D, dtype=torch.float16, device=dev)
     vc = torch.zeros_like(kc)
     qkv = torch.empty(S, N, dtype=torch.float16, device=dev)
-    qv = qkv.view(S, hq + 2 * hkv, D)
+    q_wide = torch.empty(S, N, dtype=torch.float16, device=dev)  # q_out shares q's row stride
+    dims = g.attn.make_dims(hq, hkv, S, 1e-6)
+    vp = ctypes.c_void_p
 
     def unfused():
+        # the reference's pair: GEMM into the f16 activation, then the fused
+        # kernel reading q/k/v straight out of it (row stride N)
         torch.matmul(x, w.t(), out=qkv)
-        g.qk_norm_rope_kv_prefill(qv[:, :hq], qv[:, hq:hq + hkv], qv[:, hq + hkv:], ones, ones, table,
-                                  q_out, kc, vc, 0, 1e-6)
+        st = g.lib().grout_qk_norm_rope_kv_prefill(
+            vp(qkv.data_ptr()), vp(qkv.data_ptr() + hq * D * 2), vp(qkv.data_ptr() + (hq + hkv) * D * 2),
+            N, N, vp(ones.data_ptr()), vp(ones.data_ptr()), vp(table.data_ptr()), vp(q_wide.data_ptr()),
+            vp(kc.data_ptr()), vp(vc.data_ptr()), S * D, 0, S, ctypes.byref(dims),
+            vp(torch.cuda.current_stream().cuda_stream))
+        if st != 0:
+            raise RuntimeError(g.lib().grout_attn_last_error().decode())
 
     flops = 2.0 * S * hidden * N
     res = {"workload": "QKV projection S=4096, 5120 -> 10240, + norm/RoPE/KV write", "gemm_flops": flops}
