@@ -44,6 +44,9 @@ __device__ __forceinline__ uint4 ldg16(const void* p) {
   return __ldg(reinterpret_cast<const uint4*>(p));
 }
 
+// kPaged: K/V rows go to a page pool (page_table); the contiguous
+// instantiation carries no page lookup.
+template <bool kPaged>
 __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const NormRopeArgs a) {
   const int j = threadIdx.x & 7;  // lane within the octet
   const unsigned mask = 0xFFu << (threadIdx.x & 24);
@@ -72,7 +75,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const NormRopeArgs
         dst = a.q_out + ((int64_t)s * a.hq + hh) * kHeadDim;
       } else {
         int64_t off = (int64_t)s * a.cache_batch_stride + kh * a.cache_head_stride + pos * kHeadDim;
-        if (a.page_table) {
+        if (kPaged) {
           const int64_t pg = pos / a.page_size;
           const int32_t page = a.page_table[(int64_t)s * a.table_stride + pg];
           if (page < 0 || page >= a.num_pages) {
@@ -94,7 +97,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const NormRopeArgs
         src = a.k + (int64_t)s * a.kv_row_stride + (int64_t)kh * kHeadDim;
         vsrc = a.v + (int64_t)s * a.kv_row_stride + (int64_t)kh * kHeadDim;
         int64_t off = kh * a.cache_head_stride + pos * kHeadDim;
-        if (a.page_table) {
+        if (kPaged) {
           const int64_t pg = pos / a.page_size;
           const int32_t page = a.page_table[pg];
           if (page < 0 || page >= a.num_pages) {
@@ -166,7 +169,10 @@ cudaError_t launch_qk_norm_rope_kv(const NormRopeArgs& a, int num_sms, cudaStrea
   int64_t blocks = (ntask + per_block - 1) / per_block;
   const int64_t cap = (int64_t)num_sms * 8;  // 8 resident 256-thread blocks per SM
   if (blocks > cap) blocks = cap;
-  qk_norm_rope_kv_kernel<<<(unsigned)blocks, 256, 0, s>>>(a);
+  if (a.page_table)
+    qk_norm_rope_kv_kernel<true><<<(unsigned)blocks, 256, 0, s>>>(a);
+  else
+    qk_norm_rope_kv_kernel<false><<<(unsigned)blocks, 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 
