@@ -129,6 +129,26 @@ def test_prefill_split_heuristic(L):
     assert L.grout_attn_prefill_splitk_workspace_bytes(1, 2048, 8, 3) == 8 * 8 * 3 * 2 * 128 * 130 * 4
 
 
+def test_splitk_and_qkv_validation_before_launch(L):
+    p = ctypes.c_void_p(0x10000)
+    d = _dims()
+    st = L.grout_attn_prefill_splitk(None, 2, ctypes.byref(d), None, 0, None)
+    assert st == 1 and "args" in _err(L)
+    args = attn.PrefillVarlenArgs(0x10000, 0x10000, 64 * 128, 100, 0x10000, 0x10000, 0, 128,
+                                  4096 * 128, 4096, None, None, None, 2, 100)
+    st = L.grout_attn_prefill_splitk(ctypes.byref(args), 3, ctypes.byref(d), None, 0, None)
+    assert st == 1 and "cu_seqlens_q" in _err(L)
+    args.batch = 1
+    st = L.grout_attn_prefill_splitk(ctypes.byref(args), 9, ctypes.byref(d), None, 0, None)
+    assert st == 1 and "num_splits" in _err(L)
+    st = L.grout_qkv_proj_norm_rope_kv_prefill(p, 5120, p, 5100, p, p, p, p, p, p, 4096 * 128, None,
+                                               0, 16, ctypes.byref(d), None)
+    assert st == 1 and "hidden" in _err(L)
+    st = L.grout_qkv_proj_norm_rope_kv_prefill(p, 5120, p, 5120, p, p, p, p, p, p, 4096 * 128, None,
+                                               4090, 16, ctypes.byref(d), None)
+    assert st == 1 and "exceeds max_seq" in _err(L)
+
+
 def test_init_without_gpu_fails_cleanly(L):
     import torch
     if torch.cuda.is_available():
