@@ -49,7 +49,8 @@ class L2Flush:
         self.w.fill_(float(self.i))
         self.sink = self.r.sum()
 # DRAM bytes (read + write) of one prefill_kernel launch on this workload,
-# from the ncu capture summarised in profiles/prefill_kernel_qwen3_32b_s4096.md
+# taken from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum);
+# bench.py cannot read DRAM counters itself, so the line labels it as such.
 PREFILL_TRAFFIC_BYTES = 83_973_632 + 25_476_352
 
 
@@ -256,6 +257,55 @@ def e2e_pipelined(args, g, dev, stream, host_in, host_out, dev_in0, out0, consts
     return e0.elapsed_time(e1)
 
 
+def copy_ceiling_ms(dev, host_in, host_out, dist, reps=5):
+    """The e2e step's host-copy bound on this rank, all ranks copying at once:
+    the same pinned H2D (inputs) and D2H (output) bytes as one e2e step, on
+    two streams like e2e_pipelined, without any compute.  Median ms."""
+    import torch
+    dev_in = [torch.empty_like(h, device=dev) for h in host_in]
+    dev_out = torch.empty_like(host_out, device=dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ts = []
+    for _ in range(reps):
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        cur = torch.cuda.current_stream(dev)
+        e0.record(cur)
+        s_in.wait_stream(cur)
+        s_out.wait_stream(cur)
+        with torch.cuda.stream(s_in):
+            for d, h in zip(dev_in, host_in):
+                d.copy_(h, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            host_out.copy_(dev_out, non_blocking=True)
+        cur.wait_stream(s_in)
+        cur.wait_stream(s_out)
+        e1.record(cur)
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    return statistics.median(ts)
+
+
+def hbm_read_gbs(dev, nbytes=4 << 30, reps=5):
+    """Read-only HBM rate: a torch sum over an nbytes f32 buffer (decode is a
+    pure read stream, which the copy-based peak understates)."""
+    import torch
+    x = torch.ones(nbytes // 4, dtype=torch.float32, device=dev)
+    ts = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        x.sum()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    del x
+    torch.cuda.empty_cache()
+    return nbytes / (min(ts) * 1e-3) / 1e9
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import grout_b200 as g
@@ -321,7 +371,9 @@ def run_ours(args, rank, world, local_rank):
     e2e_ms = e2e_pipelined(args, g, dev, stream, (hq_, hk_, hv_), host_out,
                            (dq, dk, dv), out, (dqw, dkw, table, q_out, kc, vc), dist)
 
-    step_ms, e2e_ms, attn_ms, fused_ms = reduce_max([step_ms, e2e_ms, attn_ms, fused_ms], dist, dev)
+    copy_ms = copy_ceiling_ms(dev, (hq_, hk_, hv_), host_out, dist)
+    step_ms, e2e_ms, attn_ms, fused_ms, copy_ms = reduce_max(
+        [step_ms, e2e_ms, attn_ms, fused_ms, copy_ms], dist, dev)
     ragged = None if args.no_ragged else ragged_c4(args, dev, rank, world, dist)
     c5 = None if args.no_e2e_decode else config5(args, rank, world, dist)
     if rank != 0:
@@ -346,7 +398,11 @@ def run_ours(args, rank, world, local_rank):
                      "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": round(achieved / pk["bf16_tflops"], 4),
                      "peak_src": pk["src"] + " bf16 burst (dense f16 == bf16 rate on B200)",
-                     "traffic": PREFILL_TRAFFIC_BYTES, "kernel_ms": round(attn_ms, 4),
+                     "traffic": PREFILL_TRAFFIC_BYTES,
+                     "traffic_src": "ncu capture of prefill_kernel on this workload (not measured "
+                                    "in this run); algorithmic bytes Q+K+V+O = 151 MB, the O "
+                                    "writes still in L2 at kernel end are not counted by DRAM",
+                     "kernel_ms": round(attn_ms, 4),
                      "algorithmic_flops": flops},
         "fused_norm_rope_kv": {"bound": "hbm", "ms": round(fused_ms, 4),
                                "gbs": round(fused_bytes(S) / (fused_ms * 1e-3) / 1e9, 1),
@@ -356,6 +412,12 @@ def run_ours(args, rank, world, local_rank):
                 "unit": "TFLOP/s", "h2d_bytes_per_step": int(hq_.numel() * 2 + hk_.numel() * 2 + hv_.numel() * 2),
                 "d2h_bytes_per_step": int(host_out.numel() * 2),
                 "ms_per_step": round(e2e_ms / args.steps, 4),
+                # the host-copy bound: one step's H2D + D2H bytes copied by
+                # every rank at once with no compute (max over ranks)
+                "copy_ceiling": {"ms_per_step": round(copy_ms, 4),
+                                 "value": round(job_tflops(flops, 1, world, copy_ms), 2),
+                                 "unit": "TFLOP/s",
+                                 "e2e_frac_of_ceiling": round(copy_ms / (e2e_ms / args.steps), 4)},
                 "path": "grout_b200.qk_norm_rope_kv_prefill + attention_prefill, pinned host buffers; "
                         "each step's H2D and D2H copies on their own streams, overlapping the "
                         "neighbouring steps' compute"},
@@ -363,11 +425,13 @@ def run_ours(args, rank, world, local_rank):
         "clocks": clk.summary(),
     }
     if ragged is not None:
-        ragged["frac"] = round(ragged["tflops"] / pk["bf16_tflops"], 4)
+        # per GPU: the aggregate over N ranks against N GPUs' peak
+        ragged["frac_per_gpu"] = round(ragged["tflops"] / (world * pk["bf16_tflops"]), 4)
         line["ragged_c4"] = ragged
     if c5 is not None:
         line["e2e_decode_c5"] = c5
     if world == 1 and not args.no_decode:
+        pk["hbm_read_gbs"] = round(hbm_read_gbs(dev), 1)
         line["decode"] = decode_grid(args, dev, pk)
         line["decode_paged"] = decode_paged_cells(args, dev, pk)
         line["prefill_splitk"] = prefill_splitk_cell(args, dev, pk)
@@ -494,12 +558,15 @@ def decode_grid(args, dev, pk):
         nbytes = B * (2 * hkv * L * D * 2 + 2 * hq * D * 2)
         gbs = nbytes / (us * 1e-6) / 1e9
         cells.append({"B": B, "L": L, "hq": hq, "splits": nks, "us": round(us, 2),
-                      "gbs": round(gbs, 1), "frac": round(gbs / pk["hbm_gbs"], 4)})
+                      "gbs": round(gbs, 1), "frac": round(gbs / pk["hbm_gbs"], 4),
+                      "frac_read": round(gbs / pk["hbm_read_gbs"], 4)})
         del kc, vc
         torch.cuda.empty_cache()
     g.check_device_error()
     big = [c for c in cells if c["B"] * c["L"] >= 8 * 8192]
-    return {"unit": "GB/s", "peak_gbs": pk["hbm_gbs"], "cells": cells,
+    return {"unit": "GB/s", "peak_gbs": pk["hbm_gbs"], "read_peak_gbs": pk["hbm_read_gbs"],
+            "frac": "of the measured copy peak; frac_read: of the read-only rate measured "
+                    "in this run (torch sum over 4 GiB)", "cells": cells,
             "mean_frac_large_cells": round(statistics.mean(c["frac"] for c in big), 4)}
 
 
@@ -670,6 +737,30 @@ def emit(line):
     os.write(_STDOUT_FD, (json.dumps(line) + "\n").encode())
 
 
+def profile_case_qkv_proj():
+    """Qwen3-32B prefill QKV projection + fused norm/RoPE/KV write, S = 4096:
+    two launches on cuda:0, so `ncu -k <kernel> -s 1 -c 1` captures one warm
+    launch."""
+    import torch
+    import grout_b200 as g
+    g.init(0)
+    hidden, N = 5120, (HQ + 2 * HKV) * D
+    dev = torch.device("cuda", 0)
+    x = torch.randn(S, hidden, device=dev).half()
+    w = (torch.randn(N, hidden, device=dev) * 0.02).half()
+    ones = torch.ones(D, dtype=torch.float16, device=dev)
+    table = g.rope_table(THETA, S, dev)
+    q_out = torch.empty(S, HQ, D, dtype=torch.float16, device=dev)
+    kc = torch.zeros(HKV, S, D, dtype=torch.float16, device=dev)
+    vc = torch.zeros_like(kc)
+    for _ in range(2):
+        g.qkv_proj_norm_rope_kv_prefill(x, w, ones, ones, table, q_out, kc, vc, 0, EPS)
+    torch.cuda.synchronize()
+    g.check_device_error()
+
+
+PROFILE_CASES = {"qkv_proj": profile_case_qkv_proj}
+
 _STDOUT_FD = 1
 
 
@@ -698,8 +789,14 @@ def main():
                     help="skip the prefill workload (decode grid only; for profiling)")
     ap.add_argument("--decode-cells", default="",
                     help="comma list BxL of config-3 cells (default: the full grid + config 1)")
+    ap.add_argument("--profile-case", choices=sorted(PROFILE_CASES),
+                    help="run one small single-kernel workload for an ncu capture and exit "
+                         "(prints no JSON line)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.profile_case:
+        PROFILE_CASES[args.profile_case]()
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -722,6 +819,7 @@ def main():
         g.init(local_rank)
         if rank == 0:
             pk = peaks()
+            pk["hbm_read_gbs"] = round(hbm_read_gbs(dev), 1)
             line = {"decode": decode_grid(args, dev, pk), "decode_paged": decode_paged_cells(args, dev, pk),
                     "prefill_splitk": prefill_splitk_cell(args, dev, pk),
                     "qkv_proj_epilogue": qkv_proj_cell(args, dev, pk)}

@@ -7,7 +7,9 @@ and the build script (build.py).
 """
 from .attn import (  # noqa: F401
     GroutError,
+    add_rms_norm,
     attention_decode,
+    attention_decode_fused,
     attention_decode_paged,
     attention_prefill,
     attention_prefill_paged,
@@ -25,6 +27,7 @@ from .attn import (  # noqa: F401
     qk_norm_rope_kv_prefill_paged,
     qkv_proj_norm_rope_kv_prefill,
     rope_table,
+    silu_mul,
 )
 
 __version__ = "0.1.0"

@@ -30,6 +30,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libgrout_attn.so")
 
 HEAD_DIM = 128
+CLUSTER_MAX_SPLITS = 16
 FLAG_DECODE_SCALE_F16 = 0x1
 
 _STATUS = {0: "OK", 1: "INVALID_ARG", 2: "UNSUPPORTED", 3: "CUDA", 4: "DEVICE"}
@@ -115,6 +116,10 @@ SIGNATURES = {
                                          _vp, _sz, _vp]),
     "grout_attn_decode_ex": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i32, _i32, _i32,
                                             _DIMS, _vp, _sz, _vp]),
+    "grout_attn_decode_fused": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp,
+                                               _vp, _i32, _i32, _DIMS, _vp, _sz, _vp]),
+    "grout_add_rms_norm": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _f32, _vp]),
+    "grout_silu_mul": (ctypes.c_int, [_vp, _vp, _i32, _i32, _vp]),
     "grout_tp_comm_create": (ctypes.c_int, [_i32, _i32, ctypes.POINTER(_vp), _vp]),
     "grout_tp_comm_connect": (ctypes.c_int, [_vp, _i32, _vp]),
     "grout_tp_comm_destroy": (None, [_vp]),
@@ -407,7 +412,8 @@ def decode_workspace_bytes(batch, max_kv_len, num_q_heads, num_kv_heads, max_seq
     if num_splits is None:
         dims = make_dims(num_q_heads, num_kv_heads, max_seq)
         return lib().grout_attn_decode_workspace_bytes(batch, max_kv_len, ctypes.byref(dims))
-    return 0 if num_splits <= 1 else batch * num_q_heads * num_splits * 129 * 4
+    # up to CLUSTER_MAX_SPLITS splits merge inside a thread-block cluster
+    return 0 if num_splits <= CLUSTER_MAX_SPLITS else batch * num_q_heads * num_splits * 129 * 4
 
 
 def attention_decode(q, k_cache, v_cache, position, out, max_kv_len, workspace=None,
@@ -440,6 +446,70 @@ def attention_decode(q, k_cache, v_cache, position, out, max_kv_len, workspace=N
         _ptr(q), _ptr(k_cache), _ptr(v_cache), hkv * max_seq * HEAD_DIM, max_seq * HEAD_DIM,
         _ptr(position), _ptr(out), B, int(max_kv_len), int(num_splits), ctypes.byref(dims),
         _ptr(workspace), ws_bytes, _stream(q)))
+    return out
+
+
+def attention_decode_fused(qkv, q_norm_w, k_norm_w, rope_table, k_cache, v_cache, position, out,
+                           max_kv_len, eps, q_out=None, workspace=None, qk_scale=None,
+                           scale_f16=True):
+    """One decode step of a layer's attention in one kernel: the fused Q/K
+    RMSNorm + RoPE + KV-cache write of qk_norm_rope_kv_decode followed by
+    attention_decode (same bits as that pair).  qkv [B, (Hq + 2 Hkv) * 128];
+    caches [B, Hkv, max_seq, 128] (or [Hkv, max_seq, 128] for B = 1); out
+    [B, Hq, 128]; q_out (optional) receives the normalised, rotated query."""
+    for t, n in ((qkv, "qkv"), (q_norm_w, "q_norm_w"), (k_norm_w, "k_norm_w"),
+                 (k_cache, "k_cache"), (v_cache, "v_cache"), (out, "out")):
+        _f16_cuda(t, n)
+    B, hq = out.shape[0], out.shape[1]
+    kc = k_cache if k_cache.dim() == 4 else k_cache.unsqueeze(0)
+    _need(kc.shape[0] >= B and kc.shape[3] == HEAD_DIM, f"k_cache shape mismatch: {tuple(k_cache.shape)}")
+    _need(v_cache.shape == k_cache.shape, "v_cache shape mismatch")
+    hkv, max_seq = kc.shape[1], kc.shape[2]
+    _need(qkv.numel() == B * (hq + 2 * hkv) * HEAD_DIM, f"qkv shape mismatch: {tuple(qkv.shape)}")
+    if q_out is not None:
+        _f16_cuda(q_out, "q_out")
+        _need(q_out.numel() == B * hq * HEAD_DIM, "q_out shape mismatch")
+    _need(position.is_cuda and position.dtype in (torch.int32, torch.uint32) and position.numel() >= B,
+          "position must be a device int32/uint32 tensor with one entry per sequence")
+    dims = make_dims(hq, hkv, max_seq, rms_eps=eps, qk_scale=qk_scale,
+                     flags=FLAG_DECODE_SCALE_F16 if scale_f16 else 0)
+    need = lib().grout_attn_decode_workspace_bytes(B, int(max_kv_len), ctypes.byref(dims))
+    if need and workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=qkv.device)
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    _check(lib().grout_attn_decode_fused(
+        _ptr(qkv), _ptr(q_norm_w), _ptr(k_norm_w), _ptr(rope_table), _ptr(q_out), _ptr(k_cache),
+        _ptr(v_cache), hkv * max_seq * HEAD_DIM, max_seq * HEAD_DIM, _ptr(position), _ptr(out), B,
+        int(max_kv_len), ctypes.byref(dims), _ptr(workspace), ws_bytes, _stream(qkv)))
+    return out
+
+
+def add_rms_norm(x, weight, out, eps, residual=None, residual_out=None):
+    """out = rmsnorm(x + residual) * weight (f32 math, one f16 rounding);
+    residual_out (optional) receives f16(x + residual).  x, residual, out,
+    residual_out [rows, n]; weight [n]."""
+    for t, n in ((x, "x"), (weight, "weight"), (out, "out")):
+        _f16_cuda(t, n)
+    n = weight.numel()
+    rows = x.numel() // n
+    _need(x.numel() == rows * n and out.numel() == x.numel(), "add_rms_norm shape mismatch")
+    for t, nm in ((residual, "residual"), (residual_out, "residual_out")):
+        if t is not None:
+            _f16_cuda(t, nm)
+            _need(t.numel() == x.numel(), f"{nm} shape mismatch")
+    _check(lib().grout_add_rms_norm(_ptr(x), _ptr(residual), _ptr(weight), _ptr(out),
+                                    _ptr(residual_out), rows, n, float(eps), _stream(x)))
+    return out
+
+
+def silu_mul(gate_up, out):
+    """out [rows, n] = silu(gate) * up for gate_up [rows, 2n] = [gate | up]."""
+    _f16_cuda(gate_up, "gate_up")
+    _f16_cuda(out, "out")
+    n = gate_up.shape[-1] // 2
+    rows = gate_up.numel() // (2 * n)
+    _need(out.numel() == rows * n, "silu_mul shape mismatch")
+    _check(lib().grout_silu_mul(_ptr(gate_up), _ptr(out), rows, n, _stream(gate_up)))
     return out
 
 
@@ -575,7 +645,7 @@ def attention_decode_noalloc(q, k_cache, v_cache, position, out, max_kv_len, qk_
     """attention_decode without a workspace, for callers that cannot allocate
     device memory (a fixed memory plan, an FFI host with no allocator, code
     inside a stream capture).  The split-K scratch is the library's own
-    fixed device array (grout_attn_decode_noalloc_max_bytes(), 1 MiB); larger
+    fixed device array (grout_attn_decode_noalloc_max_bytes(), 512 KiB); larger
     shapes raise GroutError.  Calls that can overlap on the GPU share that
     array and race; make the first call on a device before any capture."""
     for t, n in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache"), (out, "out")):

@@ -119,7 +119,9 @@ grout_status encode_map(CUtensorMap* m, const void* base, int rank, const uint64
 // Split count for decode: about one CTA per SM in total (measured on B200:
 // longer splits stream better than many short ones, and every extra split
 // costs a partial write and its share of the merge), never fewer than 256
-// keys per split.
+// keys per split.  Counts just above the cluster limit come down to it when
+// the launch still covers most SMs, so the splits merge inside a cluster
+// (no workspace, no merge launch).
 int choose_splits(int32_t batch, int32_t max_kv_len, int32_t hkv, int num_sms) {
   const int keys = 64;
   const int tiles = (max_kv_len + keys - 1) / keys;
@@ -127,6 +129,8 @@ int choose_splits(int32_t batch, int32_t max_kv_len, int32_t hkv, int num_sms) {
   int64_t nks = (num_sms + units - 1) / units;
   const int64_t hi = std::max(1, tiles / 4);
   if (nks > hi) nks = hi;
+  if (nks > kDecodeMaxClusterSplits && units * kDecodeMaxClusterSplits >= (num_sms * 5) / 8)
+    nks = kDecodeMaxClusterSplits;
   if (nks < 1) nks = 1;
   if (nks > 1024) nks = 1024;
   return (int)nks;
@@ -493,8 +497,10 @@ int32_t grout_attn_decode_splits(int32_t batch, int32_t max_kv_len, const grout_
   return choose_splits(batch, max_kv_len, dims->num_kv_heads, sms);
 }
 
+// Split counts up to kDecodeMaxClusterSplits merge inside a thread-block
+// cluster and need no workspace.
 static size_t decode_ws_bytes(int32_t batch, int32_t hq, int32_t nks) {
-  if (nks <= 1) return 0;
+  if (nks <= kDecodeMaxClusterSplits) return 0;
   return (size_t)batch * hq * nks * (128 + 1) * sizeof(float);
 }
 
@@ -504,17 +510,21 @@ size_t grout_attn_decode_workspace_bytes(int32_t batch, int32_t max_kv_len,
   return decode_ws_bytes(batch, dims->num_q_heads, grout_attn_decode_splits(batch, max_kv_len, dims));
 }
 
-grout_status grout_attn_decode_ex(const void* q, const void* k_cache, const void* v_cache,
+// Shared by the decode entry points: validation of the cache / workspace
+// arguments, the tensor maps and the launch.  `fused` (may be null) carries
+// the fused norm/RoPE/KV-write inputs; then q is unused.
+static grout_status decode_common(const void* q, const void* k_cache, const void* v_cache,
                                   int64_t cache_batch_stride, int64_t cache_head_stride,
                                   const uint32_t* d_position, void* out, int32_t batch,
                                   int32_t max_kv_len, int32_t num_splits,
                                   const grout_attn_dims* dims, void* workspace,
-                                  size_t workspace_bytes, grout_stream_t stream) {
+                                  size_t workspace_bytes, DecodeArgs* fused,
+                                  grout_stream_t stream) {
   grout_status st = check_dims(dims, 8);
   if (st != GROUT_OK) return st;
   if (batch < 0) return fail(GROUT_ERR_INVALID_ARG, "batch=%d", batch);
   if (batch == 0) return GROUT_OK;  // empty call: nothing to read or write
-  const void* ptrs[] = {q, k_cache, v_cache, out};
+  const void* ptrs[] = {fused ? k_cache : q, k_cache, v_cache, out};
   for (const void* p : ptrs) {
     if (!p) return fail(GROUT_ERR_INVALID_ARG, "null pointer argument");
     if (!aligned16(p)) return fail(GROUT_ERR_INVALID_ARG, "pointer %p is not 16-byte aligned", p);
@@ -547,10 +557,10 @@ grout_status grout_attn_decode_ex(const void* q, const void* k_cache, const void
   if (st != GROUT_OK) return st;
   st = encode_map(&tv, v_cache, 4, dk, sk, bk, "v_cache");
   if (st != GROUT_OK) return st;
-  DecodeArgs a{};
+  DecodeArgs a = fused ? *fused : DecodeArgs{};
   a.q = static_cast<const __half*>(q);
   a.out = static_cast<__half*>(out);
-  a.part_o = static_cast<float*>(workspace);
+  a.part_o = need ? static_cast<float*>(workspace) : nullptr;
   a.part_lse = need ? static_cast<float*>(workspace) + (size_t)batch * dims->num_q_heads * num_splits * 128
                     : nullptr;
   a.d_position = d_position;
@@ -558,12 +568,60 @@ grout_status grout_attn_decode_ex(const void* q, const void* k_cache, const void
   a.hq = dims->num_q_heads;
   a.hkv = dims->num_kv_heads;
   a.nks = num_splits;
+  a.cluster = num_splits > 1 && need == 0;
+  a.max_seq = dims->max_seq;
   float scale = qk_scale(dims);
   if (dims->flags & GROUT_FLAG_DECODE_SCALE_F16) scale = __half2float(__float2half_rn(scale));
   a.scale_log2 = scale / logf(2.0f);
   a.err = ds->err;
+  a.k_cache = static_cast<__half*>(const_cast<void*>(k_cache));
+  a.v_cache = static_cast<__half*>(const_cast<void*>(v_cache));
+  a.cache_batch_stride = batch > 1 ? cache_batch_stride : 0;
+  a.cache_head_stride = cache_head_stride;
   CUDA_TRY(launch_decode(a, tk, tv, reinterpret_cast<cudaStream_t>(stream)));
   return GROUT_OK;
+}
+
+grout_status grout_attn_decode_ex(const void* q, const void* k_cache, const void* v_cache,
+                                  int64_t cache_batch_stride, int64_t cache_head_stride,
+                                  const uint32_t* d_position, void* out, int32_t batch,
+                                  int32_t max_kv_len, int32_t num_splits,
+                                  const grout_attn_dims* dims, void* workspace,
+                                  size_t workspace_bytes, grout_stream_t stream) {
+  return decode_common(q, k_cache, v_cache, cache_batch_stride, cache_head_stride, d_position,
+                       out, batch, max_kv_len, num_splits, dims, workspace, workspace_bytes,
+                       nullptr, stream);
+}
+
+grout_status grout_attn_decode_fused(const void* qkv, const void* q_norm_w, const void* k_norm_w,
+                                     const float* rope_table, void* q_out, void* k_cache,
+                                     void* v_cache, int64_t cache_batch_stride,
+                                     int64_t cache_head_stride, const uint32_t* d_position,
+                                     void* out, int32_t batch, int32_t max_kv_len,
+                                     const grout_attn_dims* dims, void* workspace,
+                                     size_t workspace_bytes, grout_stream_t stream) {
+  grout_status st = check_dims(dims, 8);
+  if (st != GROUT_OK) return st;
+  if (batch <= 0) return batch == 0 ? GROUT_OK : fail(GROUT_ERR_INVALID_ARG, "batch=%d", batch);
+  const void* ptrs[] = {qkv, q_norm_w, k_norm_w, rope_table};
+  for (const void* p : ptrs) {
+    if (!p) return fail(GROUT_ERR_INVALID_ARG, "null pointer argument");
+    if (!aligned16(p)) return fail(GROUT_ERR_INVALID_ARG, "pointer %p is not 16-byte aligned", p);
+  }
+  if (q_out && !aligned16(q_out))
+    return fail(GROUT_ERR_INVALID_ARG, "pointer %p is not 16-byte aligned", q_out);
+  DecodeArgs f{};
+  f.qkv = static_cast<const __half*>(qkv);
+  f.qkv_row_stride = (int64_t)(dims->num_q_heads + 2 * dims->num_kv_heads) * 128;
+  f.q_w = static_cast<const __half*>(q_norm_w);
+  f.k_w = static_cast<const __half*>(k_norm_w);
+  f.table = rope_table;
+  f.eps = dims->rms_eps;
+  f.q_out = static_cast<__half*>(q_out);
+  return decode_common(nullptr, k_cache, v_cache, cache_batch_stride, cache_head_stride,
+                       d_position, out, batch, max_kv_len,
+                       grout_attn_decode_splits(batch, max_kv_len, dims), dims, workspace,
+                       workspace_bytes, &f, stream);
 }
 
 grout_status grout_attn_decode(const void* q, const void* k_cache, const void* v_cache,
@@ -578,6 +636,48 @@ grout_status grout_attn_decode(const void* q, const void* k_cache, const void* v
   return grout_attn_decode_ex(q, k_cache, v_cache, cache_batch_stride, cache_head_stride,
                               d_position, out, batch, max_kv_len, nks, dims, workspace,
                               workspace_bytes, stream);
+}
+
+/* ------------------------------------------------------- decode-graph glue */
+
+grout_status grout_add_rms_norm(const void* x, const void* residual, const void* weight, void* out,
+                                void* residual_out, int32_t rows, int32_t n, float eps,
+                                grout_stream_t stream) {
+  if (rows < 0 || n <= 0 || n % 8 || n > 16384)
+    return fail(GROUT_ERR_INVALID_ARG, "add_rms_norm: rows=%d n=%d (n a multiple of 8, <= 16384)",
+                rows, n);
+  if (rows == 0) return GROUT_OK;
+  const void* ptrs[] = {x, weight, out};
+  for (const void* p : ptrs) {
+    if (!p) return fail(GROUT_ERR_INVALID_ARG, "null pointer argument");
+    if (!aligned16(p)) return fail(GROUT_ERR_INVALID_ARG, "pointer %p is not 16-byte aligned", p);
+  }
+  if ((residual && !aligned16(residual)) || (residual_out && !aligned16(residual_out)))
+    return fail(GROUT_ERR_INVALID_ARG, "residual pointers must be 16-byte aligned");
+  DeviceState* ds;
+  grout_status st = current_state(&ds);
+  if (st != GROUT_OK) return st;
+  CUDA_TRY(launch_add_rms_norm(static_cast<const __half*>(x), static_cast<const __half*>(residual),
+                               static_cast<const __half*>(weight), static_cast<__half*>(out),
+                               static_cast<__half*>(residual_out), rows, n, eps,
+                               reinterpret_cast<cudaStream_t>(stream)));
+  return GROUT_OK;
+}
+
+grout_status grout_silu_mul(const void* gate_up, void* out, int32_t rows, int32_t n,
+                            grout_stream_t stream) {
+  if (rows < 0 || n <= 0 || n % 8)
+    return fail(GROUT_ERR_INVALID_ARG, "silu_mul: rows=%d n=%d (n a multiple of 8)", rows, n);
+  if (rows == 0) return GROUT_OK;
+  if (!gate_up || !out) return fail(GROUT_ERR_INVALID_ARG, "null pointer argument");
+  if (!aligned16(gate_up) || !aligned16(out))
+    return fail(GROUT_ERR_INVALID_ARG, "gate_up and out must be 16-byte aligned");
+  DeviceState* ds;
+  grout_status st = current_state(&ds);
+  if (st != GROUT_OK) return st;
+  CUDA_TRY(launch_silu_mul(static_cast<const __half*>(gate_up), static_cast<__half*>(out), rows, n,
+                           ds->num_sms, reinterpret_cast<cudaStream_t>(stream)));
+  return GROUT_OK;
 }
 
 /* ----------------------------------------------------------- paged caches */
@@ -705,7 +805,7 @@ grout_status grout_attn_decode_paged(const void* q, const void* k_pages, const v
   DecodeArgs a{};
   a.q = static_cast<const __half*>(q);
   a.out = static_cast<__half*>(out);
-  a.part_o = static_cast<float*>(workspace);
+  a.part_o = need ? static_cast<float*>(workspace) : nullptr;
   a.part_lse = need ? static_cast<float*>(workspace) + (size_t)batch * dims->num_q_heads * num_splits * 128
                     : nullptr;
   a.d_position = d_position;
@@ -713,6 +813,8 @@ grout_status grout_attn_decode_paged(const void* q, const void* k_pages, const v
   a.hq = dims->num_q_heads;
   a.hkv = dims->num_kv_heads;
   a.nks = num_splits;
+  a.cluster = num_splits > 1 && need == 0;
+  a.max_seq = dims->max_seq;
   float scale = qk_scale(dims);
   if (dims->flags & GROUT_FLAG_DECODE_SCALE_F16) scale = __half2float(__float2half_rn(scale));
   a.scale_log2 = scale / logf(2.0f);

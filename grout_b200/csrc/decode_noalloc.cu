@@ -8,7 +8,7 @@
 // fixed array in this module's global memory instead of a caller buffer.
 //
 // The array is a file-scope __device__ object: every GPU that loads this
-// library holds kNoAllocScratchBytes of it until the process exits.  In host
+// library holds kNoAllocScratchBytes (512 KiB) of it until the process exits.  In host
 // code its name is only a host-side stand-in, so the kernels receive the
 // device address obtained with cudaGetSymbolAddress, once per device, with
 // that device current.
@@ -17,8 +17,8 @@
 // can overlap on the GPU (different streams without ordering between them)
 // race on it; calls on one stream, or otherwise ordered, are safe.  The array
 // keeps the previous call's contents; the decode kernel writes every scratch
-// entry it later reads (empty splits write 0 and -inf), so nothing needs
-// clearing between calls.
+// entry it later reads (empty or skipped splits write 0 and -inf), so nothing
+// needs clearing between calls.
 #include <cstdio>
 #include <mutex>
 
@@ -27,7 +27,13 @@
 
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = 1u << 20;  // 1 MiB per device
+// 512 KiB per device.  Decode needs split-K scratch only when one KV head
+// and sequence get more than 16 splits (up to 16 merge inside a cluster),
+// i.e. for few (sequence, KV head) pairs over long contexts: the automatic
+// split count then keeps about one CTA per SM, so the scratch is about
+// SMs * G * 129 * 4 bytes (611 KB at G = 8 on 148 SMs) or less when the
+// context caps the splits.  Shapes above the limit are rejected.
+constexpr size_t kNoAllocScratchBytes = 512u << 10;
 
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 

@@ -50,18 +50,39 @@ struct NormRopeArgs {
 
 cudaError_t launch_qk_norm_rope_kv(const NormRopeArgs& a, int num_sms, cudaStream_t s);
 
+// Splits of one (kv head, sequence) that decode merges inside a thread-block
+// cluster (distributed shared memory) instead of a workspace + merge launch.
+constexpr int kDecodeMaxClusterSplits = 16;
+
 struct DecodeArgs {
-  const __half* q;      // [B][hq][128]
+  const __half* q;      // [B][hq][128] (unfused)
   __half* out;          // [B][hq][128]
-  float* part_o;        // [B][hq][nks][128] (nks > 1)
-  float* part_lse;      // [B][hq][nks]      (nks > 1)
+  float* part_o;        // [B][hq][nks][128] (nks > 1, no cluster)
+  float* part_lse;      // [B][hq][nks]      (nks > 1, no cluster)
   const uint32_t* d_position;
   int32_t batch;
   int32_t hq;
   int32_t hkv;
   int32_t nks;
+  int32_t cluster;      // nks > 1: merge in a cluster of nks CTAs (nks <= 16)
+  int32_t max_seq;      // positions >= max_seq are rejected on the device
   float scale_log2;
   int* err;
+  // Fused norm/RoPE/KV write (qkv != null): qkv [B][(hq + 2 hkv) * 128] rows
+  // (row stride qkv_row_stride), norm weights, RoPE table; q_out optional;
+  // the new K/V rows go to the caches at position d_position[b]
+  // (contiguous: b * cache_batch_stride + kh * cache_head_stride + pos * 128).
+  const __half* qkv;
+  int64_t qkv_row_stride;
+  const __half* q_w;
+  const __half* k_w;
+  const float* table;
+  float eps;
+  __half* q_out;
+  __half* k_cache;
+  __half* v_cache;
+  int64_t cache_batch_stride;
+  int64_t cache_head_stride;
   // Paged cache (page_table != null): the maps are {128, page_size, hkv,
   // num_pages}; key row r of sequence b is row r % page_size of page
   // page_table[b * table_stride + r / page_size].
@@ -140,5 +161,12 @@ struct QkvGemmArgs {
 cudaError_t launch_qkv_gemm(const QkvGemmArgs& a, const CUtensorMap& tm_x, const CUtensorMap& tm_w,
                             int num_sms, cudaStream_t s);
 cudaError_t qkv_gemm_set_attributes();
+
+// Decode-graph glue (glue.cu).
+cudaError_t launch_add_rms_norm(const __half* x, const __half* residual, const __half* w,
+                                __half* out, __half* residual_out, int rows, int n, float eps,
+                                cudaStream_t s);
+cudaError_t launch_silu_mul(const __half* gate_up, __half* out, int rows, int n, int num_sms,
+                            cudaStream_t s);
 
 }  // namespace grout

@@ -4,168 +4,129 @@
 // (reference src/kernels.rs:4845-5168, 5180-5452).  HBM-bound: every byte of
 // q/k/v is read once and every output byte written once.
 //
-// Mapping: one octet (8 lanes) per 128-element head row, so a warp works on
-// four rows at once.  Lane j of the octet owns the RoPE pairs i = 8j..8j+7,
-// i.e. x[8j..8j+8) ("lo") and x[64+8j..64+8j+8) ("hi"): rotate-half needs no
-// shuffle, every access is 16 bytes per lane, and an octet's load covers two
-// 128-byte segments.  The arithmetic is pinned so that the CPU oracle
-// reproduces it bit for bit: no FMA contraction (explicit _rn intrinsics), a
-// fixed sum order (lane sum ((t0+t1)+(t2+t3))+((t4+t5)+(t6+t7)), then a
-// xor-butterfly 4,2,1), rsqrt as a correctly rounded reciprocal of a
-// correctly rounded sqrt, and cos/sin read from a table of correctly rounded
-// values of the reference's f32 angle.
+// Mapping: one octet (8 lanes) per 128-element head row (norm_rope.cuh holds
+// the row arithmetic, pinned so that the CPU oracle reproduces it bit for
+// bit); a warp takes 16 rows of one token at a time.
 #include "internal.h"
+#include "norm_rope.cuh"
 #include "ptx.cuh"
 
 namespace grout {
+namespace {
 
-__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
-    float2 v = __half22float2(h);
-    f[2 * i] = v.x;
-    f[2 * i + 1] = v.y;
-  }
-}
+constexpr int kSlabRows = 16;  // head rows of one token per warp task (4 per octet)
 
-__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
-  uint32_t w[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
-    w[i] = *reinterpret_cast<uint32_t*>(&h);
-  }
-  return make_uint4(w[0], w[1], w[2], w[3]);
-}
-
-__device__ __forceinline__ uint4 ldg16(const void* p) {
-  return __ldg(reinterpret_cast<const uint4*>(p));
-}
-
+// Row layout of one token: rows [0, hq) are Q heads (normalised with q_w),
+// [hq, hq + hkv) K heads (k_w), [hq + hkv, hq + 2 hkv) V heads (copied).
+//
+// A warp task is (token, slab of 16 rows); octet o of the warp takes rows
+// slab*16 + 4i + o, i < 4, issuing all four rows' loads before any math.  The
+// norm weights live in registers for the whole kernel and the token's cos/sin
+// row is loaded once per task, so per row only the row itself is read.
 // kPaged: K/V rows go to a page pool (page_table); the contiguous
 // instantiation carries no page lookup.
 template <bool kPaged>
 __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const NormRopeArgs a) {
   const int j = threadIdx.x & 7;  // lane within the octet
+  const int octet = (threadIdx.x >> 3) & 3;
   const unsigned mask = 0xFFu << (threadIdx.x & 24);
-  const uint32_t heads = (uint32_t)(a.hq + a.hkv);
-  const uint32_t ntask = (uint32_t)a.rows * heads;
-  const uint32_t step = (gridDim.x * blockDim.x) >> 3;
-  for (uint32_t task = (blockIdx.x * blockDim.x + threadIdx.x) >> 3; task < ntask; task += step) {
-    const uint32_t s = task / heads;
-    const int hh = (int)(task - s * heads);
-    const bool is_q = hh < a.hq;
-    const int kh = hh - a.hq;
-    const __half* src;
-    const __half* vsrc = nullptr;
-    __half* dst;
-    __half* vdst = nullptr;
+  const int R = a.hq + 2 * a.hkv;
+  const int slabs = (R + kSlabRows - 1) / kSlabRows;
+  const uint32_t ntask = (uint32_t)a.rows * (uint32_t)slabs;
+  const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
+
+  float qwl[8], qwh[8], kwl[8], kwh[8];
+  unpack8(ldg16(a.q_w + 8 * j), qwl);
+  unpack8(ldg16(a.q_w + 64 + 8 * j), qwh);
+  unpack8(ldg16(a.k_w + 8 * j), kwl);
+  unpack8(ldg16(a.k_w + 64 + 8 * j), kwh);
+
+  for (uint32_t task = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; task < ntask; task += warps) {
+    const uint32_t s = task / (uint32_t)slabs;
+    const int r0 = (int)(task - s * (uint32_t)slabs) * kSlabRows;
     int64_t pos;
+    const __half* qsrc;      // this token's Q / K / V head-0 rows
+    const __half* ksrc;
+    const __half* vsrc;
+    __half* qdst;
+    int64_t kv_off;          // element offset of this token's K/V row of head 0
+    int64_t kv_head_stride;  // elements between KV heads in the cache
     if (a.decode) {
       pos = a.d_position[s];
       if (pos >= a.max_seq) {
-        if (j == 0 && hh == 0 && a.err) atomicCAS(a.err, 0, DEV_ERR_POSITION);
+        if (r0 == 0 && (threadIdx.x & 31) == 0 && a.err) atomicCAS(a.err, 0, DEV_ERR_POSITION);
         continue;
       }
-      const __half* row = a.q + (int64_t)s * a.q_row_stride;
-      src = row + (int64_t)hh * kHeadDim;
-      if (is_q) {
-        dst = a.q_out + ((int64_t)s * a.hq + hh) * kHeadDim;
-      } else {
-        int64_t off = (int64_t)s * a.cache_batch_stride + kh * a.cache_head_stride + pos * kHeadDim;
-        if (kPaged) {
-          const int64_t pg = pos / a.page_size;
-          const int32_t page = a.page_table[(int64_t)s * a.table_stride + pg];
-          if (page < 0 || page >= a.num_pages) {
-            if (j == 0 && a.err) atomicCAS(a.err, 0, DEV_ERR_PAGE);
-            continue;
-          }
-          off = ((int64_t)page * a.hkv + kh) * a.page_size * kHeadDim + (pos - pg * a.page_size) * kHeadDim;
-        }
-        dst = a.k_cache + off;
-        vdst = a.v_cache + off;
-        vsrc = row + (int64_t)(a.hq + a.hkv + kh) * kHeadDim;
-      }
+      qsrc = a.q + (int64_t)s * a.q_row_stride;
+      ksrc = qsrc + (int64_t)a.hq * kHeadDim;
+      vsrc = ksrc + (int64_t)a.hkv * kHeadDim;
+      qdst = a.q_out + (int64_t)s * a.hq * kHeadDim;
+      kv_off = (int64_t)s * a.cache_batch_stride + pos * kHeadDim;
     } else {
       pos = (int64_t)a.pos0 + s;
-      if (is_q) {
-        src = a.q + (int64_t)s * a.q_row_stride + (int64_t)hh * kHeadDim;
-        dst = a.q_out + (int64_t)s * a.q_row_stride + (int64_t)hh * kHeadDim;
-      } else {
-        src = a.k + (int64_t)s * a.kv_row_stride + (int64_t)kh * kHeadDim;
-        vsrc = a.v + (int64_t)s * a.kv_row_stride + (int64_t)kh * kHeadDim;
-        int64_t off = kh * a.cache_head_stride + pos * kHeadDim;
-        if (kPaged) {
-          const int64_t pg = pos / a.page_size;
-          const int32_t page = a.page_table[pg];
-          if (page < 0 || page >= a.num_pages) {
-            if (j == 0 && a.err) atomicCAS(a.err, 0, DEV_ERR_PAGE);
-            continue;
-          }
-          off = ((int64_t)page * a.hkv + kh) * a.page_size * kHeadDim + (pos - pg * a.page_size) * kHeadDim;
-        }
-        dst = a.k_cache + off;
-        vdst = a.v_cache + off;
+      qsrc = a.q + (int64_t)s * a.q_row_stride;
+      ksrc = a.k + (int64_t)s * a.kv_row_stride;
+      vsrc = a.v + (int64_t)s * a.kv_row_stride;
+      qdst = a.q_out + (int64_t)s * a.q_row_stride;
+      kv_off = pos * kHeadDim;
+    }
+    kv_head_stride = a.cache_head_stride;
+    bool kv_ok = true;
+    if (kPaged) {
+      const int64_t pg = pos / a.page_size;
+      const int32_t page = a.page_table[(a.decode ? (int64_t)s * a.table_stride : 0) + pg];
+      kv_ok = page >= 0 && page < a.num_pages;
+      kv_off = (int64_t)page * a.hkv * a.page_size * kHeadDim + (pos - pg * a.page_size) * kHeadDim;
+      kv_head_stride = (int64_t)a.page_size * kHeadDim;
+      if (!kv_ok && r0 + kSlabRows > a.hq && (threadIdx.x & 31) == 0 && a.err)
+        atomicCAS(a.err, 0, DEV_ERR_PAGE);
+    }
+    // Issue every load of the slab first.
+    uint4 xl[4], xh[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = r0 + 4 * i + octet;
+      const __half* src = r < a.hq ? qsrc + (int64_t)r * kHeadDim
+                        : r < a.hq + a.hkv ? ksrc + (int64_t)(r - a.hq) * kHeadDim
+                                           : vsrc + (int64_t)(r - a.hq - a.hkv) * kHeadDim;
+      if (r < R) {
+        xl[i] = ldg16(src + 8 * j);
+        xh[i] = ldg16(src + 64 + 8 * j);
       }
     }
-    // Issue every load of the row first.
-    const uint4 xl = ldg16(src + 8 * j);
-    const uint4 xh = ldg16(src + 64 + 8 * j);
-    uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
-    if (vsrc) {
-      v0 = ldg16(vsrc + 8 * j);
-      v1 = ldg16(vsrc + 64 + 8 * j);
-    }
-    const __half* w = is_q ? a.q_w : a.k_w;
-    const uint4 wl4 = ldg16(w + 8 * j);
-    const uint4 wh4 = ldg16(w + 64 + 8 * j);
-    const float* trow = a.table + pos * kHeadDim;
-    const float4 c0 = __ldg(reinterpret_cast<const float4*>(trow + 8 * j));
-    const float4 c1 = __ldg(reinterpret_cast<const float4*>(trow + 8 * j + 4));
-    const float4 s0 = __ldg(reinterpret_cast<const float4*>(trow + 64 + 8 * j));
-    const float4 s1 = __ldg(reinterpret_cast<const float4*>(trow + 64 + 8 * j + 4));
-    if (vsrc) {  // V: verbatim copy
-      *reinterpret_cast<uint4*>(vdst + 8 * j) = v0;
-      *reinterpret_cast<uint4*>(vdst + 64 + 8 * j) = v1;
-    }
-    float lo[8], hi[8], wl[8], wh[8];
-    unpack8(xl, lo);
-    unpack8(xh, hi);
-    unpack8(wl4, wl);
-    unpack8(wh4, wh);
-    const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-    const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-
-    float t[8];
+    float cs[8], sn[8];
+    if (r0 < a.hq + a.hkv) load_cos_sin(a.table + pos * kHeadDim, j, cs, sn);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) t[e] = __fadd_rn(__fmul_rn(lo[e], lo[e]), __fmul_rn(hi[e], hi[e]));
-    float ss = __fadd_rn(__fadd_rn(__fadd_rn(t[0], t[1]), __fadd_rn(t[2], t[3])),
-                         __fadd_rn(__fadd_rn(t[4], t[5]), __fadd_rn(t[6], t[7])));
-#pragma unroll
-    for (int off = 4; off >= 1; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(mask, ss, off, 8));
-    // ss / 128 is an exact power-of-two scaling; the correctly rounded
-    // reciprocal equals the IEEE quotient 1.0f / x.
-    const float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(ss, 0.0078125f), a.eps)));
-
-    float ylo[8], yhi[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float nlo = __fmul_rn(__fmul_rn(lo[e], inv), wl[e]);
-      const float nhi = __fmul_rn(__fmul_rn(hi[e], inv), wh[e]);
-      ylo[e] = __fsub_rn(__fmul_rn(nlo, cs[e]), __fmul_rn(nhi, sn[e]));
-      yhi[e] = __fadd_rn(__fmul_rn(nhi, cs[e]), __fmul_rn(nlo, sn[e]));
+    for (int i = 0; i < 4; ++i) {
+      const int r = r0 + 4 * i + octet;
+      if (r >= R) continue;
+      if (r >= a.hq + a.hkv) {  // V: verbatim copy
+        if (!kv_ok) continue;
+        __half* dst = a.v_cache + kv_off + (int64_t)(r - a.hq - a.hkv) * kv_head_stride;
+        *reinterpret_cast<uint4*>(dst + 8 * j) = xl[i];
+        *reinterpret_cast<uint4*>(dst + 64 + 8 * j) = xh[i];
+        continue;
+      }
+      const bool is_q = r < a.hq;
+      uint4 ylo, yhi;
+      octet_norm_rope(xl[i], xh[i], is_q ? qwl : kwl, is_q ? qwh : kwh, cs, sn, a.eps, mask, ylo,
+                      yhi);
+      __half* dst = is_q ? qdst + (int64_t)r * kHeadDim
+                         : a.k_cache + kv_off + (int64_t)(r - a.hq) * kv_head_stride;
+      if (!is_q && !kv_ok) continue;
+      *reinterpret_cast<uint4*>(dst + 8 * j) = ylo;
+      *reinterpret_cast<uint4*>(dst + 64 + 8 * j) = yhi;
     }
-    *reinterpret_cast<uint4*>(dst + 8 * j) = pack8(ylo);
-    *reinterpret_cast<uint4*>(dst + 64 + 8 * j) = pack8(yhi);
   }
 }
 
+}  // namespace
+
 cudaError_t launch_qk_norm_rope_kv(const NormRopeArgs& a, int num_sms, cudaStream_t s) {
-  const int64_t ntask = (int64_t)a.rows * (a.hq + a.hkv);
+  const int R = a.hq + 2 * a.hkv;
+  const int64_t ntask = (int64_t)a.rows * ((R + kSlabRows - 1) / kSlabRows);
   if (ntask == 0) return cudaSuccess;
-  const int per_block = 256 / 8;
+  const int per_block = 256 / 32;
   int64_t blocks = (ntask + per_block - 1) / per_block;
   const int64_t cap = (int64_t)num_sms * 8;  // 8 resident 256-thread blocks per SM
   if (blocks > cap) blocks = cap;

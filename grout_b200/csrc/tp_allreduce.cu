@@ -12,8 +12,8 @@
 //      no TMA, no multicast) and, after a CTA barrier, raises flag
 //      [rank][i] = epoch + 1 in every peer with a system-scope release store;
 //   3. it waits — bounded by a 2 s limit, after which it records a device
-//      error and writes nothing — for flag [p][i] == epoch + 1 from every
-//      peer p, then sums the partials in rank order 0..world-1 (identical
+//      error and writes nothing — for flag [p][i] >= epoch + 1 (wrap-aware)
+//      from every peer p, then sums the partials in rank order 0..world-1 (identical
 //      bits on every rank), adds the residual and writes f16.
 // The epoch is a per-CTA counter in this rank's own buffer, advanced by the
 // kernel, so one launch recorded in a CUDA graph replays correctly.  Receive
@@ -165,10 +165,11 @@ __global__ void __launch_bounds__(kThreads) gemv_allreduce_kernel(
 #pragma unroll
     for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
   }
-  if (nchunks == 0 && lane == 0)  // this warp's K slice is empty
+  if (!w) {  // exchange only: warp 0 holds the given partial (x[hidden])
+    for (int i = lane; i < nrows; i += 32) red[warp][i] = warp == 0 ? __half2float(x[r0 + i]) : 0.f;
+  } else if (nchunks == 0 && lane == 0) {  // this warp's K slice is empty
     for (int i = 0; i < nrows; ++i) red[warp][i] = 0.f;
-  if (!w && warp == 0)  // exchange only: the partial is given (x[hidden])
-    for (int i = lane; i < nrows; i += 32) red[0][i] = __half2float(x[r0 + i]);
+  }
   __syncthreads();
   // The CTA's slice of partials goes into slot [slot][rank] of every rank's
   // receive buffer.
@@ -199,7 +200,12 @@ __global__ void __launch_bounds__(kThreads) gemv_allreduce_kernel(
     for (int p = 0; p < world; ++p) {
       const unsigned* f = flags + p * kCtas + cta;
       uint32_t spins = 0;
-      while (ld_acquire_sys(f) != epoch) {
+      // A peer may already have finished this call and raised its flag for
+      // the next one (epoch + 1) before this thread looks: any value at or
+      // past this call's epoch (wrap-aware) means the slice is in place.
+      // The slot that peer writes next is the other parity, so this call's
+      // slot is still intact.
+      while ((int)(ld_acquire_sys(f) - epoch) < 0) {
         if ((++spins & 255u) == 0 && globaltimer() - t0 > kWaitTimeoutNs) {
           s_ok = 0;
           *broken = 1u;

@@ -1,10 +1,13 @@
 """Minimal tensor-parallel Qwen3 decoder that drives the attention hot path in
 context (config 5: Qwen3-32B greedy decode after an 8192-token prompt).
 
-This is the caller of the path, not a product of its own: the projections,
-norms and MLP are plain torch / cuBLAS, the collectives are NCCL; the fused
-Q/K RMSNorm + RoPE + KV write and the prefill / decode attention are this
-library's kernels, called exactly where the reference engine calls its cuTile
+This is the caller of the path, not a product of its own: the decode GEMVs
+and the prefill o_proj / MLP GEMMs are cuBLAS, the NCCL collectives (or this
+library's NVLink all-reduce) are the exchange; this library supplies the
+attention path — the prefill QKV projection with the norm/RoPE/KV write as its
+epilogue, prefill attention, and the decode step's fused norm/RoPE/KV write +
+split-K attention in one kernel — and the residual add + RMSNorm and SiLU
+product kernels around it, called where the reference engine calls its cuTile
 kernels (src/model.rs:4031-4219 prefill ops, 3494-3790 decode graph).
 
 Layout (Megatron-style, TP = world size):
@@ -41,43 +44,72 @@ class Qwen3Shape:
     theta: float = 1.0e6
 
 
-def _rms(x, w, eps):
-    xf = x.float()
-    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype) * w
+# Weight identities for the block generator: (tensor id, layer, block).
+_EMBED, _LM_HEAD, _FINAL_NORM = 0, 1, 2
+_IN_NORM, _POST_NORM, _Q_NORM, _K_NORM = 10, 11, 12, 13
+_WQ, _WK, _WV, _WO, _GATE, _UP, _DOWN = 14, 15, 16, 17, 18, 19, 20
+CHUNKS = 8  # intermediate / vocab blocks; every TP degree divides it
+
+
+def _block_seed(seed, tid, layer, block):
+    h = seed & ((1 << 61) - 1)
+    for v in (tid, layer, block):
+        h = (h * 1000003 + v + 1) % ((1 << 61) - 1)
+    return h
 
 
 class Qwen3TP:
+    """One rank of a tensor-parallel Qwen3 decoder.
+
+    Every weight is generated block by block from (seed, tensor, layer,
+    block): a query or KV head's projection rows, a head's o_proj columns,
+    one of CHUNKS slices of the intermediate or vocab dimension.  A rank
+    generates only the blocks it owns, so rank r of TP = N holds exactly the
+    slice of the TP = 1 tensors that the Megatron layout gives it, and every
+    TP degree is the same network."""
+
     def __init__(self, shape, max_seq, rank=0, world=1, group=None, device=None, seed=6,
                  fused_allreduce=True):
         self.c = c = shape
         self.rank, self.world, self.group = rank, world, group
         self.dev = device or torch.device("cuda", torch.cuda.current_device())
-        assert c.heads % world == 0 and c.kv_heads % world == 0 and c.inter % world == 0
+        assert c.heads % world == 0 and c.kv_heads % world == 0 and CHUNKS % world == 0
+        assert c.inter % CHUNKS == 0 and c.vocab % CHUNKS == 0
         self.hq, self.hkv, self.it = c.heads // world, c.kv_heads // world, c.inter // world
-        self.vshard = (c.vocab + world - 1) // world
+        self.vshard = c.vocab // world
         self.max_seq = max_seq
-        g = torch.Generator(device=self.dev).manual_seed(seed * 1000 + rank)
         D, H = c.head_dim, c.hidden
+        cpr = CHUNKS // world  # intermediate / vocab chunks per rank
+        ich, vch = c.inter // CHUNKS, c.vocab // CHUNKS
 
-        def w(*shape):
-            return (torch.randn(*shape, device=self.dev, generator=g) * 0.02).half()
+        def gen(tid, layer, block):
+            return torch.Generator(device=self.dev).manual_seed(_block_seed(seed, tid, layer, block))
 
-        def nw(n):
-            return (1.0 + 0.02 * torch.randn(n, device=self.dev, generator=g)).half()
+        def w(shape_, tid, layer, block):
+            return (torch.randn(*shape_, device=self.dev, generator=gen(tid, layer, block)) * 0.02).half()
 
-        self.embed = w(c.vocab, H) if rank == 0 else torch.empty(c.vocab, H, device=self.dev, dtype=torch.float16)
-        if world > 1:
-            torch.distributed.broadcast(self.embed, 0, group=group)
-        self.lm_head = w(self.vshard, H)
-        self.final_norm = nw(H)
+        def nw(n, tid, layer):
+            return (1.0 + 0.02 * torch.randn(n, device=self.dev, generator=gen(tid, layer, 0))).half()
+
+        def rows(tid, layer, blocks, nrows, ncols):
+            return torch.cat([w((nrows, ncols), tid, layer, b) for b in blocks], 0)
+
+        self.embed = rows(_EMBED, 0, range(CHUNKS), vch, H)  # replicated
+        self.lm_head = rows(_LM_HEAD, 0, range(rank * cpr, (rank + 1) * cpr), vch, H)
+        self.final_norm = nw(H, _FINAL_NORM, 0)
+        qh = range(rank * self.hq, (rank + 1) * self.hq)
+        kh = range(rank * self.hkv, (rank + 1) * self.hkv)
+        ch = range(rank * cpr, (rank + 1) * cpr)
         self.layers = []
-        for _ in range(c.layers):
+        for li in range(c.layers):
             L = dict(
-                in_norm=nw(H), post_norm=nw(H), q_norm=nw(D), k_norm=nw(D),
-                w_qkv=w((self.hq + 2 * self.hkv) * D, H),
-                w_o=w(H, self.hq * D),
-                w_gu=w(2 * self.it, H),
-                w_down=w(H, self.it),
+                in_norm=nw(H, _IN_NORM, li), post_norm=nw(H, _POST_NORM, li),
+                q_norm=nw(D, _Q_NORM, li), k_norm=nw(D, _K_NORM, li),
+                w_qkv=torch.cat([rows(_WQ, li, qh, D, H), rows(_WK, li, kh, D, H),
+                                 rows(_WV, li, kh, D, H)], 0),
+                w_o=torch.cat([w((H, D), _WO, li, h) for h in qh], 1),
+                w_gu=torch.cat([rows(_GATE, li, ch, ich, H), rows(_UP, li, ch, ich, H)], 0),
+                w_down=torch.cat([w((H, ich), _DOWN, li, b) for b in ch], 1),
                 k_cache=torch.zeros(self.hkv, max_seq, D, device=self.dev, dtype=torch.float16),
                 v_cache=torch.zeros(self.hkv, max_seq, D, device=self.dev, dtype=torch.float16),
             )
@@ -85,6 +117,8 @@ class Qwen3TP:
         self.rope = attn.rope_table(c.theta, max_seq, self.dev)
         self.pos = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.tok = torch.zeros(1, dtype=torch.int64, device=self.dev)
+        # final-norm hidden state of the last step (written inside the graph)
+        self.h_last = torch.zeros(1, H, device=self.dev, dtype=torch.float16)
         nks = attn.decode_workspace_bytes(1, max_seq, self.hq, self.hkv, max_seq)
         self.ws = torch.empty(max(16, nks), dtype=torch.uint8, device=self.dev)
         # Decode o_proj / down_proj (TP > 1), the faster of each measured on
@@ -98,6 +132,9 @@ class Qwen3TP:
         # decode-step buffers (fixed addresses for graph replay)
         self.q1 = torch.empty(1, self.hq, D, device=self.dev, dtype=torch.float16)
         self.o1 = torch.empty_like(self.q1)
+        # layer-0 activations of the last eager prefill / decode step, kept
+        # when trace is set (prefill/decode consistency checks)
+        self.trace = None
 
     # ---------------------------------------------------------------- helpers
     def _allreduce(self, x):
@@ -118,6 +155,25 @@ class Qwen3TP:
             return allp[:, 1].gather(0, best).long()
         return i.view(1)
 
+    # ------------------------------------------------------------- residual
+    def _norm(self, x, w, pending=None):
+        """(normed, residual stream): rmsnorm(x + pending) * w in one kernel,
+        the stream updated to x + pending when a partial is pending (the
+        reference's add_rms_norm, src/kernels.rs:4449-4600)."""
+        h = torch.empty_like(x)
+        if pending is None:
+            attn.add_rms_norm(x, w, h, self.c.eps)
+            return h, x
+        xn = torch.empty_like(x)
+        attn.add_rms_norm(pending, w, h, self.c.eps, residual=x, residual_out=xn)
+        return h, xn
+
+    def _mlp_in(self, h, L):
+        gu = F.linear(h, L["w_gu"])
+        a = torch.empty(h.shape[0], self.it, device=self.dev, dtype=torch.float16)
+        attn.silu_mul(gu, a)
+        return a
+
     # ---------------------------------------------------------------- prefill
     def prefill(self, tokens):
         """Run the prompt (eager, like the reference's StepGraph prefill):
@@ -125,64 +181,79 @@ class Qwen3TP:
         c, D = self.c, self.c.head_dim
         S = tokens.numel()
         x = self.embed[tokens]                                   # [S, H]
+        pending = None
         for L in self.layers:
-            h = _rms(x, L["in_norm"], c.eps)
-            qkv = F.linear(h, L["w_qkv"])                        # [S, (hq+2hkv)*D]
-            q = qkv[:, : self.hq * D].reshape(S, self.hq, D).contiguous()
-            k = qkv[:, self.hq * D:(self.hq + self.hkv) * D].reshape(S, self.hkv, D).contiguous()
-            v = qkv[:, (self.hq + self.hkv) * D:].reshape(S, self.hkv, D).contiguous()
-            q_out = torch.empty_like(q)
-            attn.qk_norm_rope_kv_prefill(q, k, v, L["q_norm"], L["k_norm"], self.rope, q_out,
-                                         L["k_cache"], L["v_cache"], 0, c.eps)
+            h, x = self._norm(x, L["in_norm"], pending)
+            # QKV projection with the norm/RoPE/KV write as its epilogue
+            q_out = torch.empty(S, self.hq, D, device=self.dev, dtype=torch.float16)
+            tracing = self.trace is not None and L is self.layers[0]
+            qkv = (torch.empty(S, (self.hq + 2 * self.hkv) * D, device=self.dev,
+                               dtype=torch.float16) if tracing else None)
+            attn.qkv_proj_norm_rope_kv_prefill(h, L["w_qkv"], L["q_norm"], L["k_norm"], self.rope,
+                                               q_out, L["k_cache"], L["v_cache"], 0, c.eps,
+                                               qkv_out=qkv)
             o = torch.empty_like(q_out)
             attn.attention_prefill(q_out, L["k_cache"], L["v_cache"], o, 0)
-            x = x + self._allreduce(F.linear(o.view(S, -1), L["w_o"]))
-            h = _rms(x, L["post_norm"], c.eps)
-            gu = F.linear(h, L["w_gu"])
-            a = F.silu(gu[:, : self.it]) * gu[:, self.it:]
-            x = x + self._allreduce(F.linear(a, L["w_down"]))
-        h = _rms(x[-1:], self.final_norm, c.eps)
+            if tracing:
+                self.trace["prefill"] = (qkv, o.clone())
+            p = self._allreduce(F.linear(o.view(S, -1), L["w_o"]))
+            h, x = self._norm(x, L["post_norm"], p)
+            pending = self._allreduce(F.linear(self._mlp_in(h, L), L["w_down"]))
+        h, _ = self._norm(x[-1:].contiguous(), self.final_norm, pending[-1:].contiguous())
+        self.h_last.copy_(h)
         self.pos.fill_(S)
         self.tok.copy_(self._argmax(h))
         return self.tok
 
     # ---------------------------------------------------------------- decode
+    def _attention(self, qkv, L):
+        """The decode step's fused Q/K norm + RoPE + KV write and split-K
+        attention, one kernel (grout_attn_decode_fused)."""
+        attn.attention_decode_fused(qkv, L["q_norm"], L["k_norm"], self.rope, L["k_cache"],
+                                    L["v_cache"], self.pos, self.o1, self.max_seq, self.c.eps,
+                                    workspace=self.ws)
+
     def _decode_layers(self, x, attention_only=False):
-        c, D = self.c, self.c.head_dim
+        if attention_only:
+            for L in self.layers:
+                self._attention(self._qkv_dummy, L)
+            return None
+        pending = None
         for L in self.layers:
-            h = _rms(x, L["in_norm"], c.eps) if not attention_only else x
-            qkv = F.linear(h, L["w_qkv"]) if not attention_only else self._qkv_dummy
-            attn.qk_norm_rope_kv_decode(qkv, L["q_norm"], L["k_norm"], self.rope, self.q1,
-                                        L["k_cache"], L["v_cache"], self.pos, self.hq, self.hkv,
-                                        c.eps)
-            attn.attention_decode(self.q1, L["k_cache"], L["v_cache"], self.pos, self.o1,
-                                  self.max_seq, workspace=self.ws)
-            if attention_only:
-                continue
+            h, x = self._norm(x, L["in_norm"], pending)
+            qkv = F.linear(h, L["w_qkv"])
+            self._attention(qkv, L)
+            if self.trace is not None and L is self.layers[0]:
+                self.trace["decode"] = (qkv.clone(), self.o1.clone())
             if self.comm is not None:
                 # o_proj: GEMV + all-reduce + residual in one grout kernel
                 x1 = torch.empty_like(x)
                 self.comm.gemv_allreduce(L["w_o"], self.o1, x1, residual=x)
-                x = x1
+                h, x = self._norm(x1, L["post_norm"])
             else:
-                x = x + self._allreduce(F.linear(self.o1.view(1, -1), L["w_o"]))
-            h = _rms(x, L["post_norm"], c.eps)
-            gu = F.linear(h, L["w_gu"])
-            a = (F.silu(gu[:, : self.it]) * gu[:, self.it:]).contiguous()
+                p = self._allreduce(F.linear(self.o1.view(1, -1), L["w_o"]))
+                h, x = self._norm(x, L["post_norm"], p)
+            d = F.linear(self._mlp_in(h, L), L["w_down"])
             if self.comm is not None:
                 x2 = torch.empty_like(x)
-                self.comm.allreduce(F.linear(a, L["w_down"]), x2, residual=x)
-                x = x2
+                self.comm.allreduce(d, x2, residual=x)
+                x, pending = x2, None
             else:
-                x = x + self._allreduce(F.linear(a, L["w_down"]))
-        return x
+                pending = self._allreduce(d)
+        return x, pending
 
     def _decode_step(self):
         x = self.embed[self.tok]                                 # [1, H]
-        x = self._decode_layers(x)
-        h = _rms(x, self.final_norm, self.c.eps)
+        x, pending = self._decode_layers(x)
+        h, _ = self._norm(x, self.final_norm, pending)
+        self.h_last.copy_(h)
         self.tok.copy_(self._argmax(h))
         self.pos.add_(1)
+
+    def step_eager(self):
+        """One decode step without the graph (same ops); returns the token."""
+        self._decode_step()
+        return int(self.tok.item())
 
     def capture(self):
         """Record one decode step (all layers + argmax + position += 1) into

@@ -199,7 +199,9 @@ grout_status grout_attn_prefill_splitk(const grout_prefill_varlen_args* args, in
  * batch, max_kv_len, num_kv_heads and the SM count of the current device). */
 int32_t grout_attn_decode_splits(int32_t batch, int32_t max_kv_len, const grout_attn_dims* dims);
 
-/* Workspace bytes grout_attn_decode needs (0 when one split suffices):
+/* Workspace bytes grout_attn_decode needs: 0 when the split count is at most
+ * 16 (the splits of one KV head and sequence then merge inside a thread-block
+ * cluster through distributed shared memory), else
  * batch * num_q_heads * splits * (128 + 1) * 4. */
 size_t grout_attn_decode_workspace_bytes(int32_t batch, int32_t max_kv_len,
                                          const grout_attn_dims* dims);
@@ -223,13 +225,37 @@ grout_status grout_attn_decode(const void* q, const void* k_cache, const void* v
                                size_t workspace_bytes, grout_stream_t stream);
 
 /* As grout_attn_decode with an explicit split count (1 .. 1024); workspace
- * size batch * num_q_heads * num_splits * 129 * 4 bytes when num_splits > 1. */
+ * size batch * num_q_heads * num_splits * 129 * 4 bytes when num_splits > 16
+ * (none at or below 16, where the merge runs inside a cluster). */
 grout_status grout_attn_decode_ex(const void* q, const void* k_cache, const void* v_cache,
                                   int64_t cache_batch_stride, int64_t cache_head_stride,
                                   const uint32_t* d_position, void* out, int32_t batch,
                                   int32_t max_kv_len, int32_t num_splits,
                                   const grout_attn_dims* dims, void* workspace,
                                   size_t workspace_bytes, grout_stream_t stream);
+
+/* Decode step with the fused write folded in: replaces the pair the
+ * reference launches back to back in its decode graph,
+ * qk_norm_rope_kv_decode_raw_f16 then fmha_decode_gqa_split +
+ * splitk_reduce_merge (src/model.rs:3494ff, 3728-3771), with one kernel.
+ * Inputs as grout_qk_norm_rope_kv_decode (qkv [batch][(num_q_heads +
+ * 2*num_kv_heads)*128], norm weights, RoPE table, caches, d_position);
+ * q_out [batch][num_q_heads][128] may be NULL (the normalised, rotated query
+ * is then only used inside the kernel).  Every CTA normalises and rotates its
+ * own query heads; the one whose KV range holds the new position writes that
+ * position's K and V rows into the cache before it reads them.  The cache rows,
+ * q_out and out equal grout_qk_norm_rope_kv_decode followed by
+ * grout_attn_decode bit for bit.  Split count and workspace as
+ * grout_attn_decode (grout_attn_decode_workspace_bytes).  A position >=
+ * max_seq writes nothing but a zero output row and records device error
+ * 0x200. */
+grout_status grout_attn_decode_fused(const void* qkv, const void* q_norm_w, const void* k_norm_w,
+                                     const float* rope_table, void* q_out, void* k_cache,
+                                     void* v_cache, int64_t cache_batch_stride,
+                                     int64_t cache_head_stride, const uint32_t* d_position,
+                                     void* out, int32_t batch, int32_t max_kv_len,
+                                     const grout_attn_dims* dims, void* workspace,
+                                     size_t workspace_bytes, grout_stream_t stream);
 
 /* ------------------------------ tensor-parallel GEMV + all-reduce (NVLink) */
 
@@ -275,10 +301,13 @@ grout_status grout_allreduce_residual(grout_tp_comm* comm, const void* partial,
  * owned by a planner, an FFI host without a device allocator, code already
  * inside a stream capture.  Same arguments and result as grout_attn_decode
  * without the workspace: the split-K scratch lives in a fixed array in the
- * library's device memory (grout_attn_decode_noalloc_max_bytes() = 1 MiB,
- * held on every GPU that loads the library until the process exits).  A
- * shape whose scratch (grout_attn_decode_workspace_bytes) exceeds that is
- * rejected with GROUT_ERR_INVALID_ARG.  The first call on a device resolves
+ * library's device memory (grout_attn_decode_noalloc_max_bytes() = 512 KiB,
+ * held on every GPU that loads the library until the process exits).  Only
+ * shapes with more than 16 splits per (sequence, KV head) use scratch: few
+ * sequences and KV heads over long contexts, about SMs * G * 516 bytes at
+ * most (G = num_q_heads / num_kv_heads).  A shape whose scratch
+ * (grout_attn_decode_workspace_bytes) exceeds the array is rejected with
+ * GROUT_ERR_INVALID_ARG.  The first call on a device resolves
  * the array's device address (the device must be current); make that first
  * call before any stream capture.  All calls on a device share the array:
  * calls that can overlap on the GPU (unordered streams) race; ordered calls
@@ -306,6 +335,24 @@ grout_status grout_qkv_proj_norm_rope_kv_prefill(
     const void* k_norm_w, const float* rope_table, void* q_out, void* k_cache, void* v_cache,
     int64_t cache_head_stride, void* qkv_out, int32_t position_start, int32_t seq_len,
     const grout_attn_dims* dims, grout_stream_t stream);
+
+/* ------------------------------------------------------ decode-graph glue */
+
+/* The neighbours of the attention ops in every layer of the reference's
+ * decode graph (src/model.rs:3264-3354), one kernel each.
+ *   grout_add_rms_norm: replaces add_rms_norm_f16 / add_rms_norm_decode_raw_f16
+ *     / rms_norm_f16 (src/kernels.rs:4449-4600, 1530ff).  x, residual
+ *     (NULL = none), out, residual_out (NULL = not written): [rows][n] f16;
+ *     weight [n] f16; n a multiple of 8, <= 16384.  c = x + residual in f32,
+ *     residual_out = f16(c), out = f16(c * rsqrt(sum(c^2) / n + eps) * w).
+ *   grout_silu_mul: replaces silu_mul_2d_f16 (src/kernels.rs:1497-1526).
+ *     gate_up [rows][2n] f16 (gate columns, then up columns), out [rows][n]:
+ *     out = f16(sigmoid(g) * g * u), f32 math. */
+grout_status grout_add_rms_norm(const void* x, const void* residual, const void* weight, void* out,
+                                void* residual_out, int32_t rows, int32_t n, float eps,
+                                grout_stream_t stream);
+grout_status grout_silu_mul(const void* gate_up, void* out, int32_t rows, int32_t n,
+                            grout_stream_t stream);
 
 /* ------------------------------------------------------ paged KV caches */
 

@@ -87,7 +87,8 @@ def test_validation_before_launch(L):
     d = _dims()
     st = L.grout_attn_decode_ex(p, p, p, 0, 4096 * 128, p, p, 1, 5000, 4, ctypes.byref(d), None, 0, None)
     assert st == 1 and "max_kv_len" in _err(L)
-    st = L.grout_attn_decode_ex(p, p, p, 0, 4096 * 128, p, p, 1, 4096, 4, ctypes.byref(d), None, 0, None)
+    # more than 16 splits merge through a workspace, which must be given
+    st = L.grout_attn_decode_ex(p, p, p, 0, 4096 * 128, p, p, 1, 4096, 32, ctypes.byref(d), None, 0, None)
     assert st == 1 and "workspace" in _err(L)
     d = _dims(hq=63, hkv=8)
     st = L.grout_attn_prefill(p, p, p, p, 4096 * 128, 0, 16, ctypes.byref(d), None)
@@ -168,11 +169,16 @@ def test_decode_split_heuristic(L):
             assert B * 8 * (n - 1) < 148
             if B * 8 >= 148:
                 assert n == 1
-    assert attn.decode_splits(1, 32768, 64, 8, 32768) == 19
+    # 19 splits would cover 152 SMs; 16 still cover 128 and merge in a cluster
+    assert attn.decode_splits(1, 32768, 64, 8, 32768) == 16
     assert attn.decode_splits(8, 8192, 64, 8, 32768) == 3
-    assert attn.decode_workspace_bytes(32, 8192, 64, 8, 32768) == 0
-    n = attn.decode_splits(8, 8192, 64, 8, 32768)
-    assert attn.decode_workspace_bytes(8, 8192, 64, 8, 32768) == 8 * 64 * n * 129 * 4
+    # up to 16 splits need no workspace (cluster merge)
+    for B in (1, 8, 32):
+        assert attn.decode_workspace_bytes(B, 8192, 64, 8, 32768) == 0
+    # one KV head (tensor-parallel degree 8): more splits than a cluster holds
+    n = attn.decode_splits(1, 8448, 8, 1, 8448)
+    assert n == 33
+    assert attn.decode_workspace_bytes(1, 8448, 8, 1, 8448) == 8 * n * 129 * 4
 
 
 def test_python_mirror_rejects_cpu_tensors():

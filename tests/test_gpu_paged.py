@@ -145,11 +145,26 @@ def test_bad_page_entry_is_reported_without_a_write(grout):
     with pytest.raises(grout.GroutError, match="0x201"):
         grout.check_device_error()
     assert kp.abs().sum().item() == 0 and vp.abs().sum().item() == 0
-    # decode attention over the same table: the bad tile reads zeros, reported
-    out = torch.empty(1, hq, D, dtype=torch.float16, device=dev)
-    grout.attention_decode_paged(q_out, kp, vp, ptab, pos, out, ms)
-    with pytest.raises(grout.GroutError, match="0x201"):
-        grout.check_device_error()
+    # decode attention over the same table: the tile of the bad entry is
+    # masked out (its keys get no weight) and reported, so the result equals
+    # attention over the valid tiles alone (keys 0..127) bit for bit
+    kp.copy_(torch.randn_like(kp.float()).half())
+    vp.copy_(torch.randn_like(vp.float()).half())
+    for nks in (1, 2):
+        out = torch.empty(1, hq, D, dtype=torch.float16, device=dev)
+        grout.attention_decode_paged(q_out, kp, vp, ptab, pos, out, ms, num_splits=nks)
+        with pytest.raises(grout.GroutError, match="0x201"):
+            grout.check_device_error()
+        kc = torch.cat([kp[0], kp[1]], 1).unsqueeze(0).contiguous()   # pages 0, 1 = keys 0..127
+        vc = torch.cat([vp[0], vp[1]], 1).unsqueeze(0).contiguous()
+        ref = torch.empty_like(out)
+        grout.attention_decode(q_out, kc, vc, torch.tensor([127], dtype=torch.int32, device=dev),
+                               ref, 128, num_splits=1)
+        torch.cuda.synchronize()
+        if nks == 1:
+            assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+        else:
+            assert (out.float() - ref.float()).abs().max().item() <= 2e-3
     grout.check_device_error()  # cleared
 
 

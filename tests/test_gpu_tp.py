@@ -115,6 +115,36 @@ def _worker(rank, world, port, k, mode, q):
                 q.put((rank, "skipped"))
             dist.barrier()
             return
+        if mode == "backtoback":
+            # Eight calls with no host synchronisation between them, each
+            # rank delayed by a different amount before each call, so a fast
+            # rank finishes call n and raises its call n+1 flags while a slow
+            # one is still waiting on call n.
+            steps = 8
+            ins = [_inputs(rank, k, seed=100 + s_) for s_ in range(steps)]
+            outs_d = [torch.empty(HIDDEN, device="cuda", dtype=torch.float16) for _ in range(steps)]
+            parts = [(w.float() @ x.float()).half() for w, x in ins]
+            torch.cuda.synchronize()
+            dist.barrier()
+            for s_ in range(steps):
+                torch.cuda._sleep(int(20000 * ((rank * 3 + s_ * 5) % 7)))
+                w, x = ins[s_]
+                if s_ % 2:
+                    comm.allreduce(parts[s_], outs_d[s_], residual=res)
+                else:
+                    comm.gemv_allreduce(w, x, outs_d[s_], residual=res)
+            torch.cuda.synchronize()
+            outs = []
+            for s_ in range(steps):
+                allx = [_inputs(r, k, seed=100 + s_) for r in range(world)]
+                ref = _ref([a for a, _ in allx], [b for _, b in allx], res)
+                err = (outs_d[s_].float() - ref).abs().max().item()
+                outs.append((err, _tol(ref), outs_d[s_].cpu().view(torch.int16).clone()))
+            g.check_device_error()
+            comm.close()
+            q.put((rank, outs))
+            dist.barrier()
+            return
         outs = []
         for step in range(4):
             w, x = _inputs(rank, k, seed=step)
@@ -150,22 +180,38 @@ def _spawn(world, k, mode):
     return res
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def _need(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+
+
+def _check_ranks(res, world, steps):
+    for step in range(steps):
+        tol = res[0][step][1] * (2 if step % 2 else 1)  # exchange-only sums f16-rounded partials
+        for r in range(world):
+            assert res[r][step][0] <= tol
+            assert torch.equal(res[r][step][2], res[0][step][2])  # identical bits on every rank
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("k", [4096, 12800])
-def test_gemv_allreduce_two_ranks(k):
-    res = _spawn(2, k, "sum")
-    for step in range(4):
-        e0, t0, o0 = res[0][step]
-        e1, t1, o1 = res[1][step]
-        tol = 2 * t0 if step % 2 else t0  # exchange-only sums f16-rounded partials
-        assert e0 <= tol and e1 <= tol
-        assert torch.equal(o0, o1)  # identical bits on every rank
+def test_gemv_allreduce_ranks(world, k):
+    _need(world)
+    k = k // (world // 2)  # the row-parallel shard shrinks with the TP degree
+    _check_ranks(_spawn(world, k, "sum"), world, 4)
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_gemv_allreduce_missing_peer_times_out():
-    res = _spawn(2, 4096, "timeout")
-    assert res[1] == "skipped"
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_gemv_allreduce_back_to_back_without_sync(world):
+    _need(world)
+    _check_ranks(_spawn(world, 1024, "backtoback"), world, 8)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_gemv_allreduce_missing_peer_times_out(world):
+    _need(world)
+    res = _spawn(world, 4096, "timeout")
+    assert all(res[r] == "skipped" for r in range(1, world))
     (first, second), dt = res[0]
     assert first.startswith("error:") and "0x13c" in first
     assert second.startswith("error:") and "0x13d" in second and dt < 1.0
