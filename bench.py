@@ -194,20 +194,37 @@ def cpu_baseline(rows_step=2):
 
 
 # ------------------------------------------------------------ GPU arm
-def capture(fn):
-    """Warm `fn` up on a side stream, capture it into a CUDA graph."""
+def device_times(fns, reps, flush):
+    """Median device time (ms) of each callable in `fns`, run in sequence,
+    over `reps` repetitions with an L2 flush before each.  All repetitions
+    are recorded into ONE CUDA graph with timing events between the calls
+    (event-record nodes), so an interval holds the kernels' device time only:
+    no host launch latency and no graph-launch gap (a graph replay costs
+    ~4 us before its first kernel on B200)."""
     import torch
+    cur = torch.cuda.current_stream()
     s = torch.cuda.Stream()
-    s.wait_stream(torch.cuda.current_stream())
+    s.wait_stream(cur)
     with torch.cuda.stream(s):
-        fn()
-        fn()
-    torch.cuda.current_stream().wait_stream(s)
+        for _ in range(2):
+            for fn in fns:
+                fn()
+    cur.wait_stream(s)
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(len(fns) + 1)]
+          for _ in range(reps)]
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        fn()
+        for r in range(reps):
+            flush()
+            ev[r][0].record()
+            for i, fn in enumerate(fns):
+                fn()
+                ev[r][i + 1].record()
+    graph.replay()
     torch.cuda.synchronize()
-    return graph
+    return [statistics.median(ev[r][i].elapsed_time(ev[r][i + 1]) for r in range(reps))
+            for i in range(len(fns))]
 
 
 def e2e_pipelined(args, g, dev, stream, host_in, host_out, dev_in0, out0, consts, dist):
@@ -339,23 +356,32 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     g.check_device_error()
 
-    # Each kernel is captured once into a CUDA graph (as the engine records
-    # its decode step) so the timed region holds device work only, not the
-    # Python/ctypes launch path.
-    g_fused = capture(lambda: g.qk_norm_rope_kv_prefill(dq, dk, dv, dqw, dkw, table, q_out, kc, vc, 0, EPS))
-    g_attn = capture(lambda: g.attention_prefill(q_out, kc, vc, out, 0))
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    # The K timed steps are recorded into one CUDA graph (as the engine
+    # records its decode step): per step an L2 flush, then the fused write
+    # and the prefill kernel with timing events recorded on the device
+    # between them, so the intervals hold device work only, not the
+    # Python/ctypes launch path or the graph-launch gap.
+    fns = (lambda: g.qk_norm_rope_kv_prefill(dq, dk, dv, dqw, dkw, table, q_out, kc, vc, 0, EPS),
+           lambda: g.attention_prefill(q_out, kc, vc, out, 0))
+    for fn in fns:  # capture warm-up
+        fn()
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
+          for _ in range(args.steps)]
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(args.steps):
+            flush()  # L2 flush between timed steps (outside the events)
+            ev[i][0].record()
+            fns[0]()
+            ev[i][1].record()
+            fns[1]()
+            ev[i][2].record()
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local_rank) as clk:
-        for i in range(args.steps):
-            flush()  # L2 flush between timed steps (outside the events)
-            ev[i][0].record(stream)
-            g_fused.replay()
-            ev[i][1].record(stream)
-            g_attn.replay()
-            ev[i][2].record(stream)
+        graph.replay()
         torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -393,6 +419,8 @@ def run_ours(args, rank, world, local_rank):
                                "Qwen3-32B layer, S=4096, Hq=64, Hkv=8, D=128, batch 1 per GPU",
                    "seq_len": S, "num_q_heads": HQ, "num_kv_heads": HKV, "head_dim": D,
                    "l2": "flushed between timed steps (256 MB write + 256 MB read, outside the events)",
+                   "timing": "the K steps recorded in one CUDA graph, CUDA events recorded on the "
+                             "device around each step's kernels (device time only)",
                    "parallelism": f"sequence-sharded x{world} (no collective)"},
         "roofline": {"bound": "tensor", "kernel": "prefill_kernel (tcgen05)",
                      "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
@@ -434,6 +462,8 @@ def run_ours(args, rank, world, local_rank):
         pk["hbm_read_gbs"] = round(hbm_read_gbs(dev), 1)
         line["decode"] = decode_grid(args, dev, pk)
         line["decode_paged"] = decode_paged_cells(args, dev, pk)
+        line["decode_fused"] = decode_fused_cells(args, dev, pk)
+        line["tp_gemv"] = tp_gemv_cells(args, dev, pk)
         line["prefill_splitk"] = prefill_splitk_cell(args, dev, pk)
         line["qkv_proj_epilogue"] = qkv_proj_cell(args, dev, pk)
     if world == 1 and not args.no_cpu:
@@ -453,7 +483,8 @@ def config5(args, rank, world, dist):
     r = qwen3_tp.run_config5(rank, world, None, prompt_len=args.c5_prompt,
                              gen_tokens=args.c5_tokens, shape=c,
                              barrier=dist.barrier if dist else None,
-                             fused_allreduce=not args.c5_nccl)
+                             fused_allreduce=not args.c5_nccl,
+                             gemv_impl="cublas" if args.c5_cublas else "grout")
     dev = torch.device("cuda", torch.cuda.current_device())
     vals = reduce_max([r["decode_ms"], r["prefill_ms"], r["attn_ms_per_step"]], dist, dev)
     decode_ms, prefill_ms, attn_ms = vals
@@ -473,7 +504,8 @@ def config5(args, rank, world, dist):
             "attention_share": round(attn_ms / step_ms, 4),
             "roofline_tok_s": round(roof, 1), "frac": round(args.c5_tokens / (decode_ms * 1e-3) / roof, 4),
             "bytes_per_token_per_rank": w_bytes + kv_bytes, "first_tokens": r["first_tokens"],
-            "allreduce": r["allreduce"]}
+            "stage_ms_per_token_rank0": r["stage_ms_per_step"],
+            "gemv": r["gemv"], "allreduce": r["allreduce"]}
 
 
 def ragged_c4(args, dev, rank, world, dist):
@@ -498,21 +530,12 @@ def ragged_c4(args, dev, rank, world, dist):
     dcu = torch.from_numpy(cu).to(dev)
     ks = dcu[:-1].contiguous()
     lo, hi = shard_kv_heads(hkv, world, rank)
-    graph = capture(lambda: g.attention_prefill_varlen(
-        q, k, v, out, dcu, int(lens.max()), hkv, kv_row_stride=hkv * D, kv_head_stride=D,
-        kv_rows=tot, kv_start=ks, kv_head_range=(lo, hi)))
     flush = L2Flush(dev)
-    ts = []
-    for _ in range(max(3, min(args.steps, 10))):
-        flush()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        graph.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        ts.append(e0.elapsed_time(e1))
+    (ms,) = device_times([lambda: g.attention_prefill_varlen(
+        q, k, v, out, dcu, int(lens.max()), hkv, kv_row_stride=hkv * D, kv_head_stride=D,
+        kv_rows=tot, kv_start=ks, kv_head_range=(lo, hi))], max(3, min(args.steps, 10)), flush)
     g.check_device_error()
-    (ms,) = reduce_max([statistics.median(ts)], dist, dev)
+    (ms,) = reduce_max([ms], dist, dev)
     flops = 4.0 * D * hq * float(np.sum(lens.astype(np.float64) * (lens + 1) / 2))
     return {"workload": "C4: 16 ragged sequences, L ~ U[128, 8192] (seed 5), Qwen3-8B heads 32/8",
             "tokens": tot, "lengths": lens.tolist(), "ms": round(ms, 4),
@@ -544,17 +567,9 @@ def decode_grid(args, dev, pk):
         pos = torch.full((B,), L - 1, dtype=torch.int32, device=dev)
         nks = g.decode_splits(B, L, hq, hkv, L)
         ws = torch.empty(max(16, g.decode_workspace_bytes(B, L, hq, hkv, L)), dtype=torch.uint8, device=dev)
-        graph = capture(lambda: g.attention_decode(q, kc, vc, pos, out, L, workspace=ws))
-        ts = []
-        for _ in range(reps):
-            flush()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            graph.replay()
-            e1.record()
-            torch.cuda.synchronize()
-            ts.append(e0.elapsed_time(e1))
-        us = statistics.median(ts) * 1e3
+        (ms,) = device_times([lambda: g.attention_decode(q, kc, vc, pos, out, L, workspace=ws)],
+                             reps, flush)
+        us = ms * 1e3
         nbytes = B * (2 * hkv * L * D * 2 + 2 * hq * D * 2)
         gbs = nbytes / (us * 1e-6) / 1e9
         cells.append({"B": B, "L": L, "hq": hq, "splits": nks, "us": round(us, 2),
@@ -567,7 +582,7 @@ def decode_grid(args, dev, pk):
     return {"unit": "GB/s", "peak_gbs": pk["hbm_gbs"], "read_peak_gbs": pk["hbm_read_gbs"],
             "frac": "of the measured copy peak; frac_read: of the read-only rate measured "
                     "in this run (torch sum over 4 GiB)", "cells": cells,
-            "mean_frac_large_cells": round(statistics.mean(c["frac"] for c in big), 4)}
+            "mean_frac_large_cells": round(statistics.mean(c["frac"] for c in big), 4) if big else None}
 
 
 def prefill_splitk_cell(args, dev, pk):
@@ -591,17 +606,8 @@ def prefill_splitk_cell(args, dev, pk):
                      ("split", lambda: g.attention_prefill_splitk(
                          q, k, v, out, None, S, hkv, kv_row_stride=D, kv_head_stride=S * D,
                          kv_rows=S, num_splits=nks, workspace=ws))):
-        graph = capture(fn)
-        ts = []
-        for _ in range(max(3, min(args.steps, 10))):
-            flush()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            graph.replay()
-            e1.record()
-            torch.cuda.synchronize()
-            ts.append(e0.elapsed_time(e1))
-        us = statistics.median(ts) * 1e3
+        (ms,) = device_times([fn], max(3, min(args.steps, 10)), flush)
+        us = ms * 1e3
         res[name] = {"us": round(us, 2), "tflops": round(flops / (us * 1e-6) / 1e12, 1)}
     g.check_device_error()
     return res
@@ -646,20 +652,91 @@ def qkv_proj_cell(args, dev, pk):
     for name, fn in (("fused_epilogue", lambda: g.qkv_proj_norm_rope_kv_prefill(
                          x, w, ones, ones, table, q_out, kc, vc, 0, 1e-6)),
                      ("cublas_gemm_plus_fused_kernel", unfused)):
-        graph = capture(fn)
-        ts = []
-        for _ in range(max(3, min(args.steps, 10))):
-            flush()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            graph.replay()
-            e1.record()
-            torch.cuda.synchronize()
-            ts.append(e0.elapsed_time(e1))
-        us = statistics.median(ts) * 1e3
+        (ms,) = device_times([fn], max(3, min(args.steps, 10)), flush)
+        us = ms * 1e3
         res[name] = {"us": round(us, 2), "tflops": round(flops / (us * 1e-6) / 1e12, 1)}
     g.check_device_error()
     return res
+
+
+def decode_fused_cells(args, dev, pk):
+    """One decode step of a layer's attention at config 5's shapes (8192-token
+    prompt + 256 tokens: position 8447) and config 1's: the fused write +
+    split-K attention as one kernel (grout_attn_decode_fused) against the two
+    launches it replaces (qk_norm_rope_kv_decode, then attention_decode).
+    Bytes: the KV cache read plus the QKV row in and the K/V row and output
+    out."""
+    import torch
+    import grout_b200 as g
+    flush = L2Flush(dev)
+    reps = max(3, min(args.steps, 10))
+    cells = []
+    for name, hq, hkv, L in (("C5 TP=1", 64, 8, 8448), ("C5 TP=8", 8, 1, 8448),
+                             ("C1", 32, 8, 1024)):
+        gen = torch.Generator(device=dev).manual_seed(hq + L)
+        kc = torch.randn(1, hkv, L, D, device=dev, generator=gen).half()
+        vc = torch.randn_like(kc)
+        qkv = torch.randn(1, (hq + 2 * hkv) * D, device=dev, generator=gen).half()
+        w = torch.ones(D, device=dev, dtype=torch.float16)
+        table = g.rope_table(THETA, L, dev)
+        q1 = torch.empty(1, hq, D, device=dev, dtype=torch.float16)
+        out = torch.empty_like(q1)
+        pos = torch.full((1,), L - 1, dtype=torch.int32, device=dev)
+        ws = torch.empty(max(16, g.decode_workspace_bytes(1, L, hq, hkv, L)), dtype=torch.uint8,
+                         device=dev)
+        fused, sep_w, sep_a = device_times([
+            lambda: g.attention_decode_fused(qkv, w, w, table, kc, vc, pos, out, L, EPS, workspace=ws),
+            lambda: g.qk_norm_rope_kv_decode(qkv, w, w, table, q1, kc, vc, pos, hq, hkv, EPS),
+            lambda: g.attention_decode(q1, kc, vc, pos, out, L, workspace=ws)], reps, flush)
+        nbytes = 2 * hkv * L * D * 2 + (hq + 2 * hkv) * D * 2 + 2 * hkv * D * 2 + hq * D * 2
+        cells.append({"cell": name, "hq": hq, "hkv": hkv, "L": L,
+                      "splits": g.decode_splits(1, L, hq, hkv, L),
+                      "fused_us": round(fused * 1e3, 2),
+                      "separate_us": round((sep_w + sep_a) * 1e3, 2),
+                      "fused_gbs": round(nbytes / (fused * 1e-3) / 1e9, 1),
+                      "fused_frac": round(nbytes / (fused * 1e-3) / 1e9 / pk["hbm_gbs"], 4)})
+        del kc, vc
+        torch.cuda.empty_cache()
+    g.check_device_error()
+    return {"unit": "us", "timing": "device time of one call (events recorded inside one graph)",
+            "cells": cells}
+
+
+def tp_gemv_cells(args, dev, pk):
+    """The decode GEMVs of config 5 (batch 1, f16 weights): grout_gemv (bulk
+    copies through a shared-memory ring) at the TP = 1 shapes and the
+    row-parallel grout_gemv_allreduce (one rank: the exchange is local) at the
+    TP = 8 / TP = 2 shard shapes, each against torch's cuBLAS GEMV of the
+    same shape.  Bytes: the weight matrix; frac of the measured copy peak."""
+    import torch
+    import grout_b200 as g
+    from grout_b200 import tp
+    flush = L2Flush(dev)
+    reps = max(3, min(args.steps, 10))
+    comm = tp.TPComm(0, 1, 5120, device=dev)
+    cells = []
+    for name, n, k, fused in (("qkv TP=1", 10240, 5120, False), ("o_proj TP=1", 5120, 8192, False),
+                              ("gate_up TP=1", 51200, 5120, False),
+                              ("down_proj TP=1", 5120, 25600, False),
+                              ("o_proj+allreduce TP=8", 5120, 1024, True),
+                              ("down_proj+allreduce TP=8", 5120, 3200, True),
+                              ("down_proj+allreduce TP=2", 5120, 12800, True)):
+        w = (torch.randn(n, k, device=dev) * 0.02).half()
+        x = torch.randn(k, device=dev).half()
+        out = torch.empty(n, device=dev, dtype=torch.float16)
+        y = torch.empty(1, n, device=dev, dtype=torch.float16)
+        ours = (lambda: comm.gemv_allreduce(w, x, out)) if fused else (lambda: g.gemv(w, x, out))
+        t_ours, t_cub = device_times([ours, lambda: torch.matmul(x.view(1, -1), w.t(), out=y)],
+                                     reps, flush)
+        nbytes = n * k * 2
+        cells.append({"cell": name, "n": n, "k": k, "grout_us": round(t_ours * 1e3, 2),
+                      "grout_frac": round(nbytes / (t_ours * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+                      "cublas_us": round(t_cub * 1e3, 2),
+                      "cublas_frac": round(nbytes / (t_cub * 1e-3) / 1e9 / pk["hbm_gbs"], 4)})
+        del w
+    comm.close()
+    torch.cuda.empty_cache()
+    return {"unit": "us", "cells": cells}
 
 
 def decode_paged_cells(args, dev, pk):
@@ -683,17 +760,9 @@ def decode_paged_cells(args, dev, pk):
         out = torch.empty_like(q)
         pos = torch.full((B,), L - 1, dtype=torch.int32, device=dev)
         ws = torch.empty(max(16, g.decode_workspace_bytes(B, L, hq, hkv, L)), dtype=torch.uint8, device=dev)
-        graph = capture(lambda: g.attention_decode_paged(q, kp, vp, table, pos, out, L, workspace=ws))
-        ts = []
-        for _ in range(reps):
-            flush()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            graph.replay()
-            e1.record()
-            torch.cuda.synchronize()
-            ts.append(e0.elapsed_time(e1))
-        us = statistics.median(ts) * 1e3
+        (ms,) = device_times([lambda: g.attention_decode_paged(q, kp, vp, table, pos, out, L,
+                                                               workspace=ws)], reps, flush)
+        us = ms * 1e3
         nbytes = B * (2 * hkv * L * D * 2 + 2 * hq * D * 2)
         gbs = nbytes / (us * 1e-6) / 1e9
         cells.append({"B": B, "L": L, "page_size": ps, "us": round(us, 2), "gbs": round(gbs, 1),
@@ -759,7 +828,68 @@ def profile_case_qkv_proj():
     g.check_device_error()
 
 
-PROFILE_CASES = {"qkv_proj": profile_case_qkv_proj}
+def profile_case_decode_fused():
+    """Config 5's decode step at TP = 1 (64/8 heads, position 8447): the
+    fused norm/RoPE/KV write + split-K attention, two launches."""
+    import torch
+    import grout_b200 as g
+    g.init(0)
+    dev = torch.device("cuda", 0)
+    hq, hkv, L = HQ, HKV, 8448
+    kc = torch.randn(1, hkv, L, D, device=dev).half()
+    vc = torch.randn_like(kc)
+    qkv = torch.randn(1, (hq + 2 * hkv) * D, device=dev).half()
+    w = torch.ones(D, device=dev, dtype=torch.float16)
+    table = g.rope_table(THETA, L, dev)
+    out = torch.empty(1, hq, D, device=dev, dtype=torch.float16)
+    pos = torch.full((1,), L - 1, dtype=torch.int32, device=dev)
+    for _ in range(2):
+        g.attention_decode_fused(qkv, w, w, table, kc, vc, pos, out, L, EPS)
+    torch.cuda.synchronize()
+    g.check_device_error()
+
+
+def profile_case_norm_rope():
+    """Config 2's fused Q/K norm + RoPE + KV write (S = 4096): two launches."""
+    import torch
+    import grout_b200 as g
+    g.init(0)
+    dev = torch.device("cuda", 0)
+    q = torch.randn(S, HQ, D, device=dev).half()
+    k = torch.randn(S, HKV, D, device=dev).half()
+    v = torch.randn_like(k)
+    w = torch.ones(D, device=dev, dtype=torch.float16)
+    table = g.rope_table(THETA, S, dev)
+    q_out = torch.empty_like(q)
+    kc = torch.zeros(HKV, S, D, dtype=torch.float16, device=dev)
+    vc = torch.zeros_like(kc)
+    for _ in range(2):
+        g.qk_norm_rope_kv_prefill(q, k, v, w, w, table, q_out, kc, vc, 0, EPS)
+    torch.cuda.synchronize()
+    g.check_device_error()
+
+
+def profile_case_tp_gemv():
+    """grout_gemv_allreduce on one rank at config 5's TP = 2 down_proj shard
+    (5120 x 12800): two launches."""
+    import torch
+    import grout_b200 as g
+    from grout_b200 import tp
+    g.init(0)
+    dev = torch.device("cuda", 0)
+    comm = tp.TPComm(0, 1, 5120, device=dev)
+    w = (torch.randn(5120, 12800, device=dev) * 0.02).half()
+    x = torch.randn(12800, device=dev).half()
+    out = torch.empty(5120, device=dev, dtype=torch.float16)
+    for _ in range(2):
+        comm.gemv_allreduce(w, x, out)
+    torch.cuda.synchronize()
+    g.check_device_error()
+    comm.close()
+
+
+PROFILE_CASES = {"qkv_proj": profile_case_qkv_proj, "decode_fused": profile_case_decode_fused,
+                 "norm_rope": profile_case_norm_rope, "tp_gemv": profile_case_tp_gemv}
 
 _STDOUT_FD = 1
 
@@ -785,8 +915,13 @@ def main():
     ap.add_argument("--c5-tokens", type=int, default=256)
     ap.add_argument("--c5-nccl", action="store_true",
                     help="config 5 with cuBLAS GEMV + NCCL all-reduce instead of the fused kernel")
+    ap.add_argument("--c5-cublas", action="store_true",
+                    help="config 5 with cuBLAS decode GEMVs instead of grout_gemv")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the prefill workload (decode grid only; for profiling)")
+    ap.add_argument("--only", default="",
+                    help="with --no-prefill: comma list of decode, decode_paged, decode_fused, "
+                         "tp_gemv, prefill_splitk, qkv_proj_epilogue (default: all)")
     ap.add_argument("--decode-cells", default="",
                     help="comma list BxL of config-3 cells (default: the full grid + config 1)")
     ap.add_argument("--profile-case", choices=sorted(PROFILE_CASES),
@@ -820,9 +955,12 @@ def main():
         if rank == 0:
             pk = peaks()
             pk["hbm_read_gbs"] = round(hbm_read_gbs(dev), 1)
-            line = {"decode": decode_grid(args, dev, pk), "decode_paged": decode_paged_cells(args, dev, pk),
-                    "prefill_splitk": prefill_splitk_cell(args, dev, pk),
-                    "qkv_proj_epilogue": qkv_proj_cell(args, dev, pk)}
+            parts = {"decode": decode_grid, "decode_paged": decode_paged_cells,
+                     "decode_fused": decode_fused_cells, "tp_gemv": tp_gemv_cells,
+                     "prefill_splitk": prefill_splitk_cell,
+                     "qkv_proj_epilogue": qkv_proj_cell}
+            only = args.only.split(",") if args.only else list(parts)
+            line = {k: parts[k](args, dev, pk) for k in only}
         else:
             line = None
     else:

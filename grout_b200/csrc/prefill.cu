@@ -56,7 +56,14 @@ constexpr int kOffQ = 0;                       // 2 query tiles
 constexpr int kOffKV = 2 * kTile;              // ring
 constexpr int kOffBar = kOffKV + kSlots * kTile;
 constexpr int kOffL = kOffBar + 512;           // row sums, then row maxima: [2][item parity][tile][row]
-constexpr int kSmemBytes = kOffL + 2 * 2 * 2 * 128 * 4 + 1024;
+// Schedule of a ragged batch: sequence lengths, sequences by descending
+// length, and per query-tile pair the first compacted item index.
+constexpr int kSchedMaxBatch = 1024;
+constexpr int kSchedMaxPairs = 1024;
+constexpr int kSchedMaxRounds = 1536;  // items per CTA the precomputed list holds
+constexpr int kOffSched = kOffL + 2 * 2 * 2 * 128 * 4;
+constexpr int kSmemBytes =
+    kOffSched + (2 * kSchedMaxBatch + kSchedMaxPairs + 1 + kSchedMaxRounds) * 4 + 1024;
 
 // barrier indices (phases run on across the work items of a CTA)
 constexpr int kBarQ = 0;                      // + tile: Q_t landed (TMA)
@@ -162,9 +169,11 @@ __device__ __forceinline__ void mma_ts_lo(uint32_t d, uint32_t a_tmem, uint32_t 
 
 // One work item = two 128-row query tiles of one (sequence, head); items are
 // numbered longest-first (query-tile pair descending, then head, then
-// sequence).  In round r CTA c takes item r * gridDim.x + c, or
-// r * gridDim.x + gridDim.x - 1 - c in odd rounds: the snake order evens out
-// the causal work per CTA (a plain stride leaves the first CTAs ~12% more).
+// sequence).  In round r CTA c takes entry r * gridDim.x + c of the schedule,
+// or r * gridDim.x + gridDim.x - 1 - c in odd rounds: the snake order evens
+// out the causal work per CTA (a plain stride leaves the first CTAs ~12%
+// more).  For a ragged batch the schedule skips the empty items (see
+// item_of in prefill_kernel).
 struct Item {
   int h, b, q0, S, P, ks, q_start, n_kv, n_kv0;
   int lo;   // first KV tile of this item (split-K: its range starts here)
@@ -214,9 +223,63 @@ __device__ __forceinline__ bool decode_item(const PrefillArgs& a, int idx, int n
   return true;
 }
 
-// kPaged: K/V from a page pool; kSplit: split-K partial output.  The plain
-// instantiation carries neither.
-template <bool kPaged, bool kSplit>
+// The compacted schedule of a ragged batch (see prefill_kernel), built by the
+// whole CTA into shared memory: sched = [len | ord | beg | list], list[r] =
+// this CTA's item in round r.  Returns the number of rounds.
+template <bool kSplit>
+__device__ __forceinline__ int build_schedule(const PrefillArgs& a, int n_pairs, int n_items,
+                                           int* sched) {
+  int* s_len = sched;
+  int* s_ord = s_len + kSchedMaxBatch;
+  int* s_beg = s_ord + kSchedMaxBatch;
+  int* s_list = s_beg + kSchedMaxPairs + 1;
+  for (int b = threadIdx.x; b < a.batch; b += blockDim.x) s_len[b] = a.cu_q[b + 1] - a.cu_q[b];
+  __syncthreads();
+  for (int b = threadIdx.x; b < a.batch; b += blockDim.x) {
+    const int lb = s_len[b];
+    int rank = 0;
+    for (int c = 0; c < a.batch; ++c) rank += (s_len[c] > lb) || (s_len[c] == lb && c < b);
+    s_ord[rank] = b;
+  }
+  for (int rp = threadIdx.x; rp < n_pairs; rp += blockDim.x) {
+    const int q0 = (n_pairs - 1 - rp) * 2 * kBM;
+    int cnt = 0;
+    for (int b = 0; b < a.batch; ++b) cnt += s_len[b] > q0;
+    s_beg[rp + 1] = cnt * a.hq;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    s_beg[0] = 0;
+    for (int rp = 1; rp <= n_pairs; ++rp) s_beg[rp] += s_beg[rp - 1];
+  }
+  __syncthreads();
+  const int n_sched = s_beg[n_pairs] * (kSplit ? a.nsplit : 1);
+  const int G = (int)gridDim.x, c = (int)blockIdx.x;
+  const int rounds = min((n_sched + G - 1) / G, kSchedMaxRounds);
+  for (int r = threadIdx.x; r < rounds; r += blockDim.x) {
+    const int k = r * G + ((r & 1) ? G - 1 - c : c);
+    int idx = n_items;
+    if (k < n_sched) {
+      const int ki = kSplit ? k / a.nsplit : k;
+      int lo = 0, hi = n_pairs;  // largest rp with s_beg[rp] <= ki
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (s_beg[mid] <= ki) lo = mid;
+        else hi = mid;
+      }
+      const int m = ki - s_beg[lo];
+      idx = lo * (a.hq * a.batch) + s_ord[m / a.hq] * a.hq + m % a.hq;
+      if (kSplit) idx = idx * a.nsplit + k % a.nsplit;
+    }
+    s_list[r] = idx;
+  }
+  return rounds;  // the list is published by the caller's next __syncthreads
+}
+
+// kPaged: K/V from a page pool; kSplit: split-K partial output; kCompact: a
+// ragged batch scheduled over its non-empty items.  The plain instantiation
+// carries none of them.
+template <bool kPaged, bool kSplit, bool kCompact>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
@@ -232,7 +295,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const int n_pairs = (a.max_q_len + 2 * kBM - 1) / (2 * kBM);
   const int n_items = n_pairs * a.hq * a.batch * (kSplit ? a.nsplit : 1);
-  auto item_of = [&](int r) {
+  // A ragged batch leaves holes in the (pair, sequence, head) numbering: a
+  // short sequence has no items at high pair indices.  Striding over the
+  // numbering with the holes left in gives some CTAs far more work than
+  // others (the CTA-to-item map is fixed), so for a batch the CTAs stride
+  // over the compacted list instead — the non-empty items only, still
+  // longest first: pairs descending, then sequences by descending length,
+  // then heads.  s_beg[rp] is the first compacted index of pair
+  // n_pairs - 1 - rp; sequences holding that pair are the first ones of
+  // s_ord.  Item indices handed to decode_item stay the plain numbering.
+  int* s_len = reinterpret_cast<int*>(smem + kOffSched);
+  const int* s_list = s_len + 2 * kSchedMaxBatch + kSchedMaxPairs + 1;  // this CTA's item per round
+  const int n_rounds = kCompact ? build_schedule<kSplit>(a, n_pairs, n_items, s_len) : 0;
+  // Item of this CTA in round r (n_items once the schedule is exhausted).
+  auto item_of = [&](int r) -> int {
+    if (kCompact) return r < n_rounds ? s_list[r] : n_items;
     return r * (int)gridDim.x + ((r & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x);
   };
 
@@ -736,8 +813,10 @@ __global__ void __launch_bounds__(1024) prefill_merge_kernel(const PrefillArgs a
 }  // namespace
 
 cudaError_t prefill_set_attributes() {
-  for (auto k : {prefill_kernel<false, false>, prefill_kernel<true, false>,
-                 prefill_kernel<false, true>, prefill_kernel<true, true>}) {
+  for (auto k : {prefill_kernel<false, false, false>, prefill_kernel<true, false, false>,
+                 prefill_kernel<false, true, false>, prefill_kernel<true, true, false>,
+                 prefill_kernel<false, false, true>, prefill_kernel<true, false, true>,
+                 prefill_kernel<false, true, true>, prefill_kernel<true, true, true>}) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
   }
@@ -760,14 +839,28 @@ cudaError_t launch_prefill(const PrefillArgs& a, const CUtensorMap& tm_q, const 
   }
   const int grid = (int)(n_items < num_sms[dev] ? n_items : num_sms[dev]);
   const bool paged = a.page_table != nullptr, split = a.nsplit > 1;
-  if (paged && split)
-    prefill_kernel<true, true><<<grid, kThreads, kSmemBytes, s>>>(tm_q, tm_k, tm_v, a);
-  else if (paged)
-    prefill_kernel<true, false><<<grid, kThreads, kSmemBytes, s>>>(tm_q, tm_k, tm_v, a);
-  else if (split)
-    prefill_kernel<false, true><<<grid, kThreads, kSmemBytes, s>>>(tm_q, tm_k, tm_v, a);
-  else
-    prefill_kernel<false, false><<<grid, kThreads, kSmemBytes, s>>>(tm_q, tm_k, tm_v, a);
+  // The compacted schedule pays off when a pair index holds fewer items than
+  // two rounds of CTAs (the holes then skew whole rounds): measured on B200
+  // at config 4's batch, per-rank shard time 383-412 vs 500-528 us at 8
+  // ranks (4 query heads), 1398-1410 vs 1508-1550 us at 2; with 32 query
+  // heads (512 items per pair) the plain order is 2.5 % faster.
+  const bool compact = a.cu_q != nullptr && a.batch > 1 && a.batch <= kSchedMaxBatch &&
+                       n_pairs <= kSchedMaxPairs && (n_items + grid - 1) / grid <= kSchedMaxRounds &&
+                       a.hq * a.batch < 2 * grid;
+#define GROUT_PREFILL_LAUNCH(P, SP, C) \
+  prefill_kernel<P, SP, C><<<grid, kThreads, kSmemBytes, s>>>(tm_q, tm_k, tm_v, a)
+  if (compact) {
+    if (paged && split) GROUT_PREFILL_LAUNCH(true, true, true);
+    else if (paged) GROUT_PREFILL_LAUNCH(true, false, true);
+    else if (split) GROUT_PREFILL_LAUNCH(false, true, true);
+    else GROUT_PREFILL_LAUNCH(false, false, true);
+  } else {
+    if (paged && split) GROUT_PREFILL_LAUNCH(true, true, false);
+    else if (paged) GROUT_PREFILL_LAUNCH(true, false, false);
+    else if (split) GROUT_PREFILL_LAUNCH(false, true, false);
+    else GROUT_PREFILL_LAUNCH(false, false, false);
+  }
+#undef GROUT_PREFILL_LAUNCH
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || a.nsplit <= 1) return e;
   prefill_merge_kernel<<<(unsigned)(n_items / a.nsplit * 2), 1024, 0, s>>>(a);

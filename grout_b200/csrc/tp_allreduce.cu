@@ -4,9 +4,15 @@
 // of a tensor-parallel decode step followed by the all-reduce the reference
 // would need (it is single-GPU; the split is the Megatron layout of config 5).
 // One kernel per call on every rank:
-//   1. CTA i computes rows [i*R, (i+1)*R) of its partial W_r x_r in f32
-//      (each warp a K slice of eight rows at a time, 16-byte weight loads
-//      software-pipelined one step ahead, x in shared memory);
+//   1. CTA i computes rows [i*R, (i+1)*R) of its partial W_r x_r in f32.
+//      Those rows are one contiguous block of W; a producer warp streams it
+//      through a 6-stage shared-memory ring with bulk copies (16 KB each,
+//      completion on mbarriers, ~96 KB in flight per SM), and 16 consumer
+//      warps take 32 consecutive 16-byte chunks (256 weights) at a time
+//      against x in shared memory.  256 consecutive weights touch at most
+//      two rows (K >= 256), so a warp splits its sum into those two rows and
+//      one lane adds them to the warp's own per-row slots: every sum runs in
+//      a fixed order, the partial is deterministic;
 //   2. it stores that slice into slot [epoch & 1][rank] of every peer's
 //      receive buffer (plain stores through the CUDA-IPC mapping over NVLink;
 //      no TMA, no multicast) and, after a CTA barrier, raises flag
@@ -28,6 +34,7 @@
 
 #include "../../include/grout_attn.h"
 #include "internal.h"
+#include "gemv_stream.cuh"
 #include "ptx.cuh"
 
 namespace grout {
@@ -35,10 +42,12 @@ namespace {
 
 constexpr int kMaxWorld = 8;
 constexpr int kCtas = 148;        // CTAs per call (one per SM on B200)
-constexpr int kThreads = 512;
-constexpr int kWarps = kThreads / 32;
+constexpr int kConsumers = 512;   // threads computing the GEMV
+constexpr int kWarps = kConsumers / 32;
+constexpr int kThreads = kConsumers + 32;  // + the bulk-copy producer warp
 constexpr int kMaxRowsPerCta = 56;  // hidden <= 148 * 56
 constexpr int kMaxK = 16384;      // x held in shared memory
+constexpr int kGemvSmem = kMaxK * 2 + kGemvStages * kGemvPiece;  // x | ring
 
 // Per-rank buffer layout (bytes): recv [2][world][hidden] f32 | flags
 // [world][kCtas] u32 | epoch [kCtas] u32 | broken u32 (set once any wait of
@@ -74,108 +83,57 @@ __global__ void __launch_bounds__(kThreads) gemv_allreduce_kernel(
     const PeerPtrs peers, const int rank, const int world, const int hidden, const int k,
     const __half* __restrict__ w, const __half* __restrict__ x,
     const __half* __restrict__ residual, __half* __restrict__ out, int* err) {
-  __shared__ __align__(16) __half xs[kMaxK];
+  extern __shared__ __align__(128) uint8_t gsmem[];  // x [kMaxK] f16 | ring (GEMV only)
+  __half* xs = reinterpret_cast<__half*>(gsmem);
+  uint8_t* ring = gsmem + kMaxK * 2;
+  __shared__ __align__(8) uint64_t bars[2 * kGemvStages];  // full, empty
+  __shared__ int s_abort;
   __shared__ unsigned s_epoch;
   __shared__ int s_ok;
   const int cta = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rows = (hidden + kCtas - 1) / kCtas;
   const int r0 = min(hidden, cta * rows), r1 = min(hidden, r0 + rows);
+  const int nrows = r1 - r0;
 
   unsigned char* mine = peers.base[rank];
   unsigned* epoch_p = reinterpret_cast<unsigned*>(mine + epoch_off(world, hidden)) + cta;
   volatile unsigned* broken = reinterpret_cast<unsigned*>(mine + broken_off(world, hidden));
+  __shared__ float red[kWarps][kMaxRowsPerCta];
   if (threadIdx.x == 0) {
     s_epoch = *epoch_p;
     s_ok = *broken == 0u;
+    s_abort = 0;
     if (!s_ok && err) atomicCAS(err, 0, DEV_ERR_TIMEOUT_BASE + 61);
+    if (w) gemv_init_bars(bars, kWarps);
   }
-  __syncthreads();
-  if (!s_ok) return;  // an earlier call lost step with the peers
-  if (w)
-    for (int i = threadIdx.x * 8; i < k; i += blockDim.x * 8)
+  for (int i = threadIdx.x; i < kWarps * kMaxRowsPerCta; i += blockDim.x) (&red[0][0])[i] = 0.f;
+  if (w && threadIdx.x < kConsumers)
+    for (int i = threadIdx.x * 8; i < k; i += kConsumers * 8)
       *reinterpret_cast<uint4*>(&xs[i]) = __ldg(reinterpret_cast<const uint4*>(x + i));
   __syncthreads();
+  if (!s_ok) return;  // an earlier call lost step with the peers
   const unsigned epoch = s_epoch + 1;
   const int slot = epoch & 1;
 
-  // 1. partial rows.  Warp w covers the K slice [k0, k1) of every row of
-  //    this CTA, eight rows per group; each lane holds one 16-byte chunk of
-  //    the eight rows, and the loads of the next (group, chunk) are issued
-  //    before the current one is consumed, so round trips overlap.  Warp
-  //    partials meet in shared memory and are summed in a fixed order.
-  __shared__ float red[kWarps][kMaxRowsPerCta];
-  const int nwarps = blockDim.x >> 5;
-  const int kw = ((k + nwarps - 1) / nwarps + 255) / 256 * 256;
-  const int k0 = warp * kw, k1 = min(k, k0 + kw);
-  const int nrows = r1 - r0;
-  const int ngroups = (nrows + 7) / 8;
-  const int nchunks = w ? max(0, (k1 - k0 + 255) / 256) : 0;
-  const int total = ngroups * nchunks;
-  auto load = [&](int it, uint4 (&wv)[8]) {
-    const int g = it / nchunks, ch = it - g * nchunks;
-    const int c = k0 + ch * 256 + lane * 8;
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int r = r0 + g * 8 + u;
-      if (c < k1 && r < r1) wv[u] = __ldg(reinterpret_cast<const uint4*>(w + (int64_t)r * k + c));
-      else wv[u] = make_uint4(0, 0, 0, 0);
-    }
-  };
-  uint4 cur[8], nxt[8];
-  float acc[8];
-#pragma unroll
-  for (int u = 0; u < 8; ++u) acc[u] = 0.f;
-  if (total > 0) load(0, cur);
-  for (int it = 0; it < total; ++it) {
-    if (it + 1 < total) load(it + 1, nxt);
-    const int g = it / nchunks, ch = it - g * nchunks;
-    const int c = k0 + ch * 256 + lane * 8;
-    if (c < k1) {
-      const uint4 xv = *reinterpret_cast<const uint4*>(&xs[c]);
-      const __half2* xh = reinterpret_cast<const __half2*>(&xv);
-      float xf[8];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 b = __half22float2(xh[e]);
-        xf[2 * e] = b.x;
-        xf[2 * e + 1] = b.y;
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const __half2* wh = reinterpret_cast<const __half2*>(&cur[u]);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 a = __half22float2(wh[e]);
-          acc[u] = fmaf(a.x, xf[2 * e], acc[u]);
-          acc[u] = fmaf(a.y, xf[2 * e + 1], acc[u]);
-        }
-      }
-    }
-    if (ch == nchunks - 1) {  // group done: warp-reduce its eight rows
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        float v = acc[u];
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        if (lane == 0 && g * 8 + u < nrows) red[warp][g * 8 + u] = v;
-        acc[u] = 0.f;
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
-  }
-  if (!w) {  // exchange only: warp 0 holds the given partial (x[hidden])
-    for (int i = lane; i < nrows; i += 32) red[warp][i] = warp == 0 ? __half2float(x[r0 + i]) : 0.f;
-  } else if (nchunks == 0 && lane == 0) {  // this warp's K slice is empty
-    for (int i = 0; i < nrows; ++i) red[warp][i] = 0.f;
+  // 1. partial rows: the CTA's block of W (nrows * k weights, contiguous)
+  //    through the bulk-copy ring (gemv_stream.cuh).
+  if (w) {
+    gemv_stream_rows<kWarps>(w + (int64_t)r0 * k, nrows, k, xs, ring, bars, &red[0][0],
+                             kMaxRowsPerCta, err, 62, (volatile int*)&s_abort);
+  } else if (warp == 0) {  // exchange only: the partial is given (x[hidden])
+    for (int i = lane; i < nrows; i += 32) red[0][i] = __half2float(x[r0 + i]);
   }
   __syncthreads();
+  if (s_abort) {  // a ring wait gave up (recorded): leave the peers to time out
+    if (threadIdx.x == 0) *broken = 1u;
+    return;
+  }
   // The CTA's slice of partials goes into slot [slot][rank] of every rank's
   // receive buffer.
   if (threadIdx.x < nrows) {
     float v = 0.f;
-    for (int ww = 0; ww < nwarps; ++ww) v += red[ww][threadIdx.x];
+    for (int ww = 0; ww < kWarps; ++ww) v += red[ww][threadIdx.x];
     for (int p = 0; p < world; ++p) {
       float* recv = reinterpret_cast<float*>(peers.base[p]) + ((size_t)slot * world + rank) * hidden;
       recv[r0 + threadIdx.x] = v;
@@ -279,6 +237,13 @@ grout_status grout_tp_comm_create(int32_t world, int32_t hidden, grout_tp_comm**
   static_assert(sizeof(h) == GROUT_IPC_HANDLE_BYTES, "IPC handle size");
   std::memcpy(handle_out, &h, sizeof(h));
   c->err = device_error_word();
+  e = cudaFuncSetAttribute(gemv_allreduce_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kGemvSmem);
+  if (e != cudaSuccess) {
+    cudaFree(c->local);
+    delete c;
+    return tp_fail(GROUT_ERR_CUDA, "tp comm setup", e);
+  }
   *comm = c;
   return GROUT_OK;
 }
@@ -325,15 +290,15 @@ grout_status grout_gemv_allreduce(grout_tp_comm* c, const void* w, int32_t k, co
                                   const void* residual, void* out, grout_stream_t stream) {
   if (!c || !w || !x || !out) return tp_fail(GROUT_ERR_INVALID_ARG, "null pointer argument", cudaSuccess);
   if (c->rank < 0) return tp_fail(GROUT_ERR_INVALID_ARG, "tp comm not connected", cudaSuccess);
-  if (k <= 0 || k % 8 || k > kMaxK)
+  if (k < kGemvMinK || k % 8 || k > kMaxK)
     return tp_fail(GROUT_ERR_INVALID_ARG,
-                   "gemv_allreduce: k must be a positive multiple of 8, at most 16384", cudaSuccess);
+                   "gemv_allreduce: k must be a multiple of 8 in [256, 16384]", cudaSuccess);
   const void* ptrs[] = {w, x, out};
   for (const void* p : ptrs)
     if (reinterpret_cast<uintptr_t>(p) & 15)
       return tp_fail(GROUT_ERR_INVALID_ARG, "gemv_allreduce: pointers must be 16-byte aligned",
                      cudaSuccess);
-  gemv_allreduce_kernel<<<kCtas, kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  gemv_allreduce_kernel<<<kCtas, kThreads, kGemvSmem, reinterpret_cast<cudaStream_t>(stream)>>>(
       c->peers, c->rank, c->world, c->hidden, k, static_cast<const __half*>(w),
       static_cast<const __half*>(x), static_cast<const __half*>(residual),
       static_cast<__half*>(out), c->err);

@@ -274,7 +274,7 @@ grout_status grout_attn_decode_fused(const void* qkv, const void* q_norm_w, cons
  * Per call, on every rank in the same order:
  *   out[hidden] = residual[hidden] (may be NULL) + sum over ranks of W_r x_r,
  *   W_r [hidden][k] f16 row-major (this rank's column shard), x_r [k] f16,
- *   k a multiple of 8, <= 16384, hidden <= 8288.  Peers exchange f32 partials by direct
+ *   k a multiple of 8 in [256, 16384], hidden <= 8288.  Peers exchange f32 partials by direct
  *   stores over NVLink and per-block flags; every wait is bounded (2 s,
  *   then device error 0x13c, the output is left unwritten and the comm is
  *   marked out of step: later calls return at once with device error
@@ -353,6 +353,14 @@ grout_status grout_add_rms_norm(const void* x, const void* residual, const void*
                                 grout_stream_t stream);
 grout_status grout_silu_mul(const void* gate_up, void* out, int32_t rows, int32_t n,
                             grout_stream_t stream);
+/* Decode GEMV, one token: y[n] = W x (+ residual[n], NULL = none), W [n][k]
+ * f16 row-major, x [k] f16, f32 accumulation in a fixed order, one f16
+ * rounding; k a multiple of 8 in [256, 32768].  Replaces the decode graph's
+ * cuBLAS GEMVs (src/cublas.rs:434-470; QKV, o_proj, gate/up, down_proj at
+ * src/model.rs:3248-3354): each CTA streams a contiguous block of rows with
+ * bulk copies through a shared-memory ring. */
+grout_status grout_gemv(const void* w, int32_t n, int32_t k, const void* x, const void* residual,
+                        void* y, grout_stream_t stream);
 
 /* ------------------------------------------------------ paged KV caches */
 

@@ -33,7 +33,7 @@ def _tol(ref):
 def test_gemv_allreduce_single_rank(grout):
     from grout_b200 import tp
     comm = tp.TPComm(0, 1, HIDDEN)
-    for k in (1024, 4096, 12800):
+    for k in (256, 1024, 3200, 4096, 12800):
         w, x = _inputs(0, k, seed=k)
         res = torch.randn(HIDDEN, device="cuda").half()
         out = torch.empty(HIDDEN, device="cuda", dtype=torch.float16)
