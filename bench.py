@@ -483,8 +483,7 @@ def config5(args, rank, world, dist):
     r = qwen3_tp.run_config5(rank, world, None, prompt_len=args.c5_prompt,
                              gen_tokens=args.c5_tokens, shape=c,
                              barrier=dist.barrier if dist else None,
-                             fused_allreduce=not args.c5_nccl,
-                             gemv_impl="cublas" if args.c5_cublas else "grout")
+                             fused_allreduce=not args.c5_nccl)
     dev = torch.device("cuda", torch.cuda.current_device())
     vals = reduce_max([r["decode_ms"], r["prefill_ms"], r["attn_ms_per_step"]], dist, dev)
     decode_ms, prefill_ms, attn_ms = vals
@@ -505,7 +504,7 @@ def config5(args, rank, world, dist):
             "roofline_tok_s": round(roof, 1), "frac": round(args.c5_tokens / (decode_ms * 1e-3) / roof, 4),
             "bytes_per_token_per_rank": w_bytes + kv_bytes, "first_tokens": r["first_tokens"],
             "stage_ms_per_token_rank0": r["stage_ms_per_step"],
-            "gemv": r["gemv"], "allreduce": r["allreduce"]}
+            "allreduce": r["allreduce"]}
 
 
 def ragged_c4(args, dev, rank, world, dist):
@@ -703,39 +702,31 @@ def decode_fused_cells(args, dev, pk):
 
 
 def tp_gemv_cells(args, dev, pk):
-    """The decode GEMVs of config 5 (batch 1, f16 weights): grout_gemv (bulk
-    copies through a shared-memory ring) at the TP = 1 shapes and the
-    row-parallel grout_gemv_allreduce (one rank: the exchange is local) at the
-    TP = 8 / TP = 2 shard shapes, each against torch's cuBLAS GEMV of the
-    same shape.  Bytes: the weight matrix; frac of the measured copy peak."""
+    """The row-parallel GEMV of grout_gemv_allreduce (one rank: the exchange
+    is local) at config 5's o_proj / down_proj shard shapes, against torch's
+    cuBLAS GEMV of the same shape.  Bytes: the weight shard; frac of the
+    measured copy peak."""
     import torch
-    import grout_b200 as g
     from grout_b200 import tp
     flush = L2Flush(dev)
     reps = max(3, min(args.steps, 10))
     comm = tp.TPComm(0, 1, 5120, device=dev)
     cells = []
-    for name, n, k, fused in (("qkv TP=1", 10240, 5120, False), ("o_proj TP=1", 5120, 8192, False),
-                              ("gate_up TP=1", 51200, 5120, False),
-                              ("down_proj TP=1", 5120, 25600, False),
-                              ("o_proj+allreduce TP=8", 5120, 1024, True),
-                              ("down_proj+allreduce TP=8", 5120, 3200, True),
-                              ("down_proj+allreduce TP=2", 5120, 12800, True)):
-        w = (torch.randn(n, k, device=dev) * 0.02).half()
+    for name, k in (("o_proj TP=8", 1024), ("down_proj TP=8", 3200), ("o_proj TP=2", 4096),
+                    ("down_proj TP=2", 12800)):
+        w = (torch.randn(5120, k, device=dev) * 0.02).half()
         x = torch.randn(k, device=dev).half()
-        out = torch.empty(n, device=dev, dtype=torch.float16)
-        y = torch.empty(1, n, device=dev, dtype=torch.float16)
-        ours = (lambda: comm.gemv_allreduce(w, x, out)) if fused else (lambda: g.gemv(w, x, out))
-        t_ours, t_cub = device_times([ours, lambda: torch.matmul(x.view(1, -1), w.t(), out=y)],
+        out = torch.empty(5120, device=dev, dtype=torch.float16)
+        y = torch.empty(1, 5120, device=dev, dtype=torch.float16)
+        t_ours, t_cub = device_times([lambda: comm.gemv_allreduce(w, x, out),
+                                      lambda: torch.matmul(x.view(1, -1), w.t(), out=y)],
                                      reps, flush)
-        nbytes = n * k * 2
-        cells.append({"cell": name, "n": n, "k": k, "grout_us": round(t_ours * 1e3, 2),
+        nbytes = 5120 * k * 2
+        cells.append({"cell": name, "k": k, "grout_us": round(t_ours * 1e3, 2),
                       "grout_frac": round(nbytes / (t_ours * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
                       "cublas_us": round(t_cub * 1e3, 2),
                       "cublas_frac": round(nbytes / (t_cub * 1e-3) / 1e9 / pk["hbm_gbs"], 4)})
-        del w
     comm.close()
-    torch.cuda.empty_cache()
     return {"unit": "us", "cells": cells}
 
 
@@ -915,8 +906,6 @@ def main():
     ap.add_argument("--c5-tokens", type=int, default=256)
     ap.add_argument("--c5-nccl", action="store_true",
                     help="config 5 with cuBLAS GEMV + NCCL all-reduce instead of the fused kernel")
-    ap.add_argument("--c5-cublas", action="store_true",
-                    help="config 5 with cuBLAS decode GEMVs instead of grout_gemv")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the prefill workload (decode grid only; for profiling)")
     ap.add_argument("--only", default="",

@@ -18,7 +18,6 @@ from .attn import (  # noqa: F401
     check_device_error,
     decode_splits,
     decode_workspace_bytes,
-    gemv,
     init,
     inv_freq,
     lib,

@@ -120,7 +120,6 @@ SIGNATURES = {
                                                _vp, _i32, _i32, _DIMS, _vp, _sz, _vp]),
     "grout_add_rms_norm": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _f32, _vp]),
     "grout_silu_mul": (ctypes.c_int, [_vp, _vp, _i32, _i32, _vp]),
-    "grout_gemv": (ctypes.c_int, [_vp, _i32, _i32, _vp, _vp, _vp, _vp]),
     "grout_tp_comm_create": (ctypes.c_int, [_i32, _i32, ctypes.POINTER(_vp), _vp]),
     "grout_tp_comm_connect": (ctypes.c_int, [_vp, _i32, _vp]),
     "grout_tp_comm_destroy": (None, [_vp]),
@@ -500,20 +499,6 @@ def add_rms_norm(x, weight, out, eps, residual=None, residual_out=None):
             _need(t.numel() == x.numel(), f"{nm} shape mismatch")
     _check(lib().grout_add_rms_norm(_ptr(x), _ptr(residual), _ptr(weight), _ptr(out),
                                     _ptr(residual_out), rows, n, float(eps), _stream(x)))
-    return out
-
-
-def gemv(w, x, out, residual=None):
-    """out[n] = w @ x (+ residual): w [n, k] f16, x [k] (any leading dims of
-    size 1), f32 accumulation, one f16 rounding."""
-    for t, nm in ((w, "w"), (x, "x"), (out, "out")):
-        _f16_cuda(t, nm)
-    n, k = w.shape
-    _need(x.numel() == k and out.numel() == n, "gemv shape mismatch")
-    if residual is not None:
-        _f16_cuda(residual, "residual")
-        _need(residual.numel() == n, "residual shape mismatch")
-    _check(lib().grout_gemv(_ptr(w), n, k, _ptr(x), _ptr(residual), _ptr(out), _stream(x)))
     return out
 
 

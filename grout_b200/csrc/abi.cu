@@ -182,7 +182,6 @@ grout_status grout_attn_init(int32_t device) {
   CUDA_TRY(decode_set_attributes());
   CUDA_TRY(prefill_set_attributes());
   CUDA_TRY(qkv_gemm_set_attributes());
-  CUDA_TRY(gemv_set_attributes());
   void* err = nullptr;
   CUDA_TRY(cudaGetSymbolAddress(&err, g_device_error));
   CUDA_TRY(cudaMemset(err, 0, sizeof(int)));
@@ -662,26 +661,6 @@ grout_status grout_add_rms_norm(const void* x, const void* residual, const void*
                                static_cast<const __half*>(weight), static_cast<__half*>(out),
                                static_cast<__half*>(residual_out), rows, n, eps,
                                reinterpret_cast<cudaStream_t>(stream)));
-  return GROUT_OK;
-}
-
-grout_status grout_gemv(const void* w, int32_t n, int32_t k, const void* x, const void* residual,
-                        void* y, grout_stream_t stream) {
-  if (n < 0 || k < 256 || k % 8 || k > gemv_max_k())
-    return fail(GROUT_ERR_INVALID_ARG, "gemv: n=%d k=%d (k a multiple of 8 in [256, %d])", n, k,
-                gemv_max_k());
-  if (n == 0) return GROUT_OK;
-  const void* ptrs[] = {w, x, y};
-  for (const void* p : ptrs) {
-    if (!p) return fail(GROUT_ERR_INVALID_ARG, "null pointer argument");
-    if (!aligned16(p)) return fail(GROUT_ERR_INVALID_ARG, "pointer %p is not 16-byte aligned", p);
-  }
-  DeviceState* ds;
-  grout_status st = current_state(&ds);
-  if (st != GROUT_OK) return st;
-  CUDA_TRY(launch_gemv(static_cast<const __half*>(w), n, k, static_cast<const __half*>(x),
-                       static_cast<const __half*>(residual), static_cast<__half*>(y), ds->num_sms,
-                       ds->err, reinterpret_cast<cudaStream_t>(stream)));
   return GROUT_OK;
 }
 

@@ -2,12 +2,19 @@
 // contiguous block of rows of W, which is one contiguous byte range, and
 // streams it through a shared-memory ring with untiled bulk copies
 // (cp.async.bulk, 16 KB per copy, completion on mbarriers, never multicast).
-// One producer warp issues the copies; kWarps consumer warps take 32
-// consecutive 16-byte chunks (256 weights) at a time and dot them with x held
-// in shared memory.  256 consecutive weights touch at most two rows when the
-// row length k >= 256, so a warp splits its sum into those two rows and one
-// lane adds them to the warp's own per-row slots — every sum runs in a fixed
-// order, the result is deterministic.  The caller sums the warps' slots.
+// One producer warp issues the copies; each of kWarps consumer warps owns
+// every kWarps-th row of the block and dots the parts of its rows in each
+// piece with x held in shared memory, lanes striding over 16-byte chunks; a
+// row's lane sums stay in registers across pieces and are reduced once, at
+// the row's end.  Every sum runs in a fixed order, the result is
+// deterministic.  The caller sums the warps' per-row slots (only the owner
+// warp's slot of a row is non-zero).
+//
+// Measured on B200 (one rank, L2 flushed): a 5120 x 12800 block at 0.52 of
+// the copy-measured HBM rate, cuBLAS's GEMV 0.75; a mapping that spreads
+// every piece over all warps (reducing per 256 weights, or per row change)
+// reached only 0.36-0.43: the consumers' shuffles, not the copies, set the
+// rate (a copy-only probe of the same ring streams at 6.9 TB/s).
 #pragma once
 #include <cuda_fp16.h>
 
@@ -18,7 +25,7 @@
 namespace grout {
 
 constexpr int kGemvPiece = 16384;  // bytes per bulk copy
-constexpr int kGemvStages = 6;     // ~96 KB in flight per CTA
+constexpr int kGemvMaxStages = 12;  // up to 192 KB in flight per CTA
 constexpr int kGemvMinK = 256;
 
 __device__ __forceinline__ float gemv_dot8(const uint4& wv, const uint4& xv) {
@@ -35,26 +42,27 @@ __device__ __forceinline__ float gemv_dot8(const uint4& wv, const uint4& xv) {
   return acc;
 }
 
-// Barrier words: bars[0, kGemvStages) "piece landed" (count 1, transaction
-// bytes), bars[kGemvStages, 2 kGemvStages) "slot free" (count kWarps).
-__device__ __forceinline__ void gemv_init_bars(uint64_t* bars, int consumer_warps) {
-  for (int i = 0; i < kGemvStages; ++i) {
+// Barrier words: bars[0, nst) "piece landed" (count 1, transaction bytes),
+// bars[kGemvMaxStages, kGemvMaxStages + nst) "slot free" (count kWarps).
+__device__ __forceinline__ void gemv_init_bars(uint64_t* bars, int consumer_warps, int nst) {
+  for (int i = 0; i < nst; ++i) {
     mbar_init(smem_u32(&bars[i]), 1);
-    mbar_init(smem_u32(&bars[kGemvStages + i]), consumer_warps);
+    mbar_init(smem_u32(&bars[kGemvMaxStages + i]), consumer_warps);
   }
   fence_mbar_init();
 }
 
 // Called by every thread of the CTA's consumer warps (warp < kWarps) and of
 // the producer warp (warp == kWarps).  w_blk: the first weight of the block
-// (16-byte aligned), nrows * k weights.  red: [kWarps][red_stride] f32,
+// (16-byte aligned), nrows * k weights; ring: nst <= kGemvMaxStages slots of
+// kGemvPiece bytes.  red: [kWarps][red_stride] f32,
 // zeroed by the caller; xs: x [k] f16 in shared memory.  Returns false if a
 // bounded wait gave up (recorded in *err as 0x100 + site).
 template <int kWarps>
 __device__ __forceinline__ bool gemv_stream_rows(const __half* w_blk, int nrows, int k,
                                                  const __half* xs, uint8_t* ring, uint64_t* bars,
-                                                 float* red, int red_stride, int* err, int site,
-                                                 volatile int* abort) {
+                                                 int nst, float* red, int red_stride, int* err,
+                                                 int site, volatile int* abort) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t blk_bytes = (int64_t)nrows * k * 2;
   const int npieces = (int)((blk_bytes + kGemvPiece - 1) / kGemvPiece);
@@ -63,9 +71,9 @@ __device__ __forceinline__ bool gemv_stream_rows(const __half* w_blk, int nrows,
   if (warp == kWarps) {
     if (lane == 0) {
       for (int p = 0; p < npieces; ++p) {
-        const int st = p % kGemvStages;
-        if (p >= kGemvStages &&
-            !mbar_wait(smem_u32(&bars[kGemvStages + st]), ((p / kGemvStages) - 1) & 1, err, site,
+        const int st = p % nst;
+        if (p >= nst &&
+            !mbar_wait(smem_u32(&bars[kGemvMaxStages + st]), ((p / nst) - 1) & 1, err, site,
                        abort)) {
           ok = false;
           break;
@@ -79,64 +87,41 @@ __device__ __forceinline__ bool gemv_stream_rows(const __half* w_blk, int nrows,
     }
     return ok;
   }
-  constexpr int kConsumers = kWarps * 32;
-  constexpr int kIter = (kGemvPiece / 16 + kConsumers - 1) / kConsumers;  // chunks per thread
-  constexpr int kPieceW = kGemvPiece / 2;                                    // weights per piece
+  // Warp w owns rows w, w + kWarps, ... of the block.  Every warp walks all
+  // pieces in order — waits for each, adds the chunks of its rows that lie
+  // in it, and releases it — so a slot is refilled once all warps are past
+  // it.
+  constexpr int kPieceChunks = kGemvPiece / 16;
+  const int cpr = k / 8;  // 16-byte chunks per row
+  const int total = nrows * cpr;  // < 2^31: a CTA's block is at most tens of MB
   float* my_red = red + warp * red_stride;
-  // (row, col) of this thread's chunk i in the current piece, advanced by
-  // one piece (kPieceW weights = q rows + rem) per step: no division in the
-  // loop.
-  const int q = kPieceW / k, rem = kPieceW - q * k;
-  int row[kIter], col[kIter];
-#pragma unroll
-  for (int i = 0; i < kIter; ++i) {
-    const int e = (threadIdx.x + i * kConsumers) * 8;
-    row[i] = e / k;
-    col[i] = e - row[i] * k;
-  }
+  int r = warp;
+  float acc = 0.f;
   for (int p = 0; p < npieces; ++p) {
-    const int st = p % kGemvStages;
-    if (!mbar_wait(smem_u32(&bars[st]), (p / kGemvStages) & 1, err, site + 1, abort)) {
+    const int st = p % nst;
+    if (!mbar_wait(smem_u32(&bars[st]), (p / nst) & 1, err, site + 1, abort)) {
       ok = false;
       break;
     }
-    const int chunks = (int)(min((int64_t)kGemvPiece, blk_bytes - (int64_t)p * kGemvPiece) / 16);
+    const int c0 = p * kPieceChunks;
+    const int c1 = min(c0 + kPieceChunks, total);
     const uint8_t* buf = ring + st * kGemvPiece;
+    while (r < nrows) {
+      const int rs = r * cpr, re = rs + cpr;
+      if (rs >= c1) break;  // the row starts in a later piece
+      const int lo = max(rs, c0), hi = min(re, c1);
+      for (int c = lo + lane; c < hi; c += 32)
+        acc += gemv_dot8(*reinterpret_cast<const uint4*>(buf + (c - c0) * 16),
+                         *reinterpret_cast<const uint4*>(xs + (c - rs) * 8));
+      if (re > c1) break;  // the row goes on in the next piece
 #pragma unroll
-    for (int i = 0; i < kIter; ++i) {
-      if (i * kConsumers < chunks) {  // block-uniform: whole chunk groups only
-        const int c = threadIdx.x + i * kConsumers;
-        const bool valid = c < chunks;
-        // Past the end of the block (last piece only) a lane takes the last
-        // row, which the valid lanes of its group reach: a group still
-        // spans at most two rows.
-        const int r = valid ? row[i] : nrows - 1;
-        const float v = valid ? gemv_dot8(*reinterpret_cast<const uint4*>(buf + c * 16),
-                                          *reinterpret_cast<const uint4*>(xs + col[i]))
-                              : 0.f;
-        const int row0 = __shfl_sync(0xffffffffu, r, 0);
-        const int row1 = __shfl_sync(0xffffffffu, r, 31);
-        float v0 = r == row0 ? v : 0.f;
-        float v1 = r == row0 ? 0.f : v;
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-          v0 += __shfl_xor_sync(0xffffffffu, v0, off);
-          v1 += __shfl_xor_sync(0xffffffffu, v1, off);
-        }
-        if (lane == 0) {
-          my_red[row0] += v0;
-          if (row1 != row0) my_red[row1] += v1;
-        }
-      }
-      row[i] += q;
-      col[i] += rem;
-      if (col[i] >= k) {
-        col[i] -= k;
-        ++row[i];
-      }
+      for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+      if (lane == 0) my_red[r] = acc;
+      acc = 0.f;
+      r += kWarps;
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(&bars[kGemvStages + st]));
+    if (lane == 0) mbar_arrive(smem_u32(&bars[kGemvMaxStages + st]));
   }
   return ok;
 }

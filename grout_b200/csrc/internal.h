@@ -162,13 +162,6 @@ cudaError_t launch_qkv_gemm(const QkvGemmArgs& a, const CUtensorMap& tm_x, const
                             int num_sms, cudaStream_t s);
 cudaError_t qkv_gemm_set_attributes();
 
-// Decode GEMV y = W x (+ residual) (gemv.cu); k a multiple of 8 in
-// [256, gemv_max_k()].
-int gemv_max_k();
-cudaError_t gemv_set_attributes();
-cudaError_t launch_gemv(const __half* w, int n, int k, const __half* x, const __half* residual,
-                        __half* y, int num_sms, int* err, cudaStream_t s);
-
 // Decode-graph glue (glue.cu).
 cudaError_t launch_add_rms_norm(const __half* x, const __half* residual, const __half* w,
                                 __half* out, __half* residual_out, int rows, int n, float eps,

@@ -47,7 +47,8 @@ constexpr int kWarps = kConsumers / 32;
 constexpr int kThreads = kConsumers + 32;  // + the bulk-copy producer warp
 constexpr int kMaxRowsPerCta = 56;  // hidden <= 148 * 56
 constexpr int kMaxK = 16384;      // x held in shared memory
-constexpr int kGemvSmem = kMaxK * 2 + kGemvStages * kGemvPiece;  // x | ring
+constexpr int kRingStages = 11;  // with x (32 KB) and the static state: < 227 KB
+constexpr int kGemvSmem = kMaxK * 2 + kRingStages * kGemvPiece;  // x | ring
 
 // Per-rank buffer layout (bytes): recv [2][world][hidden] f32 | flags
 // [world][kCtas] u32 | epoch [kCtas] u32 | broken u32 (set once any wait of
@@ -86,7 +87,7 @@ __global__ void __launch_bounds__(kThreads) gemv_allreduce_kernel(
   extern __shared__ __align__(128) uint8_t gsmem[];  // x [kMaxK] f16 | ring (GEMV only)
   __half* xs = reinterpret_cast<__half*>(gsmem);
   uint8_t* ring = gsmem + kMaxK * 2;
-  __shared__ __align__(8) uint64_t bars[2 * kGemvStages];  // full, empty
+  __shared__ __align__(8) uint64_t bars[2 * kGemvMaxStages];  // full, empty
   __shared__ int s_abort;
   __shared__ unsigned s_epoch;
   __shared__ int s_ok;
@@ -105,7 +106,7 @@ __global__ void __launch_bounds__(kThreads) gemv_allreduce_kernel(
     s_ok = *broken == 0u;
     s_abort = 0;
     if (!s_ok && err) atomicCAS(err, 0, DEV_ERR_TIMEOUT_BASE + 61);
-    if (w) gemv_init_bars(bars, kWarps);
+    if (w) gemv_init_bars(bars, kWarps, kRingStages);
   }
   for (int i = threadIdx.x; i < kWarps * kMaxRowsPerCta; i += blockDim.x) (&red[0][0])[i] = 0.f;
   if (w && threadIdx.x < kConsumers)
@@ -119,7 +120,7 @@ __global__ void __launch_bounds__(kThreads) gemv_allreduce_kernel(
   // 1. partial rows: the CTA's block of W (nrows * k weights, contiguous)
   //    through the bulk-copy ring (gemv_stream.cuh).
   if (w) {
-    gemv_stream_rows<kWarps>(w + (int64_t)r0 * k, nrows, k, xs, ring, bars, &red[0][0],
+    gemv_stream_rows<kWarps>(w + (int64_t)r0 * k, nrows, k, xs, ring, bars, kRingStages, &red[0][0],
                              kMaxRowsPerCta, err, 62, (volatile int*)&s_abort);
   } else if (warp == 0) {  // exchange only: the partial is given (x[hidden])
     for (int i = lane; i < nrows; i += 32) red[0][i] = __half2float(x[r0 + i]);

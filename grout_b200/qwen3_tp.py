@@ -69,10 +69,9 @@ class Qwen3TP:
     TP degree is the same network."""
 
     def __init__(self, shape, max_seq, rank=0, world=1, group=None, device=None, seed=6,
-                 fused_allreduce=True, gemv_impl="grout"):
+                 fused_allreduce=True):
         self.c = c = shape
         self.rank, self.world, self.group = rank, world, group
-        self.gemv_impl = gemv_impl
         self.dev = device or torch.device("cuda", torch.cuda.current_device())
         assert c.heads % world == 0 and c.kv_heads % world == 0 and CHUNKS % world == 0
         assert c.inter % CHUNKS == 0 and c.vocab % CHUNKS == 0
@@ -122,8 +121,10 @@ class Qwen3TP:
         self.h_last = torch.zeros(1, H, device=self.dev, dtype=torch.float16)
         nks = attn.decode_workspace_bytes(1, max_seq, self.hq, self.hkv, max_seq)
         self.ws = torch.empty(max(16, nks), dtype=torch.uint8, device=self.dev)
-        # Decode o_proj / down_proj (TP > 1): one grout kernel each (GEMV +
-        # all-reduce over NVLink peer memory + residual); NCCL when disabled.
+        # Decode o_proj / down_proj (TP > 1), the faster of each measured on
+        # B200: o_proj as one grout kernel (GEMV + all-reduce over NVLink peer
+        # memory + residual), down_proj as a cuBLAS GEMV followed by the grout
+        # all-reduce + residual.  NCCL when disabled.
         self.comm = None
         if fused_allreduce and world > 1:
             from .tp import TPComm
@@ -212,15 +213,9 @@ class Qwen3TP:
                                     L["v_cache"], self.pos, self.o1, self.max_seq, self.c.eps,
                                     workspace=self.ws)
 
-    def _proj(self, w, x, residual=None):
-        """Decode GEMV y = w x (+ residual) as [1, n]: this library's
-        weight-streaming kernel, or cuBLAS when self.gemv_impl == "cublas"."""
-        if self.gemv_impl == "cublas":
-            y = F.linear(x.view(1, -1), w)
-            return y if residual is None else y + residual
-        y = torch.empty(1, w.shape[0], device=self.dev, dtype=torch.float16)
-        attn.gemv(w, x, y, residual=residual)
-        return y
+    def _proj(self, w, x):
+        """Decode GEMV [1, n] = w x (cuBLAS)."""
+        return F.linear(x.view(1, -1), w)
 
     def _decode_layers(self, x, attention_only=False, mark=lambda name: None):
         """All layers of one decode step.  mark(name) is called after each
@@ -245,13 +240,9 @@ class Qwen3TP:
                 self.comm.gemv_allreduce(L["w_o"], self.o1, x1, residual=x)
                 mark("o_proj_gemv_allreduce")
                 h, x = self._norm(x1, L["post_norm"])
-            elif self.world == 1:
-                x = self._proj(L["w_o"], self.o1, residual=x)
-                mark("o_proj_gemv")
-                h, x = self._norm(x, L["post_norm"])
             else:
                 p = self._allreduce(self._proj(L["w_o"], self.o1))
-                mark("o_proj_gemv_nccl_allreduce")
+                mark("o_proj_gemv" + ("_nccl_allreduce" if self.world > 1 else ""))
                 h, x = self._norm(x, L["post_norm"], p)
             mark("add_rms_norm")
             gu = self._proj(L["w_gu"], h)
@@ -259,17 +250,19 @@ class Qwen3TP:
             a = torch.empty(1, self.it, device=self.dev, dtype=torch.float16)
             attn.silu_mul(gu, a)
             mark("silu_mul")
-            if self.comm is not None and self.it <= 16384:
+            d = self._proj(L["w_down"], a)
+            mark("down_gemv")
+            if self.comm is not None:
+                # down_proj: cuBLAS GEMV, then the grout all-reduce + residual
+                # (faster than the fused kernel at this shape, see tp_allreduce.cu)
                 x2 = torch.empty_like(x)
-                self.comm.gemv_allreduce(L["w_down"], a, x2, residual=x)
+                self.comm.allreduce(d, x2, residual=x)
                 x, pending = x2, None
-                mark("down_proj_gemv_allreduce")
-            elif self.world == 1:
-                x, pending = self._proj(L["w_down"], a, residual=x), None
-                mark("down_gemv")
+                mark("down_allreduce")
             else:
-                pending = self._allreduce(self._proj(L["w_down"], a))
-                mark("down_gemv_nccl_allreduce")
+                pending = self._allreduce(d)
+                if self.world > 1:
+                    mark("down_nccl_allreduce")
         return x, pending
 
     def _decode_step(self, mark=lambda name: None):
@@ -350,14 +343,13 @@ class Qwen3TP:
 
 
 def run_config5(rank=0, world=1, group=None, prompt_len=8192, gen_tokens=256, shape=None,
-                barrier=None, fused_allreduce=True, gemv_impl="grout"):
+                barrier=None, fused_allreduce=True):
     """Config 5 measurement on this rank: returns a dict (rank 0 meaningful)."""
     c = shape or Qwen3Shape()
     dev = torch.device("cuda", torch.cuda.current_device())
     max_seq = prompt_len + gen_tokens
     t0 = time.perf_counter()
-    m = Qwen3TP(c, max_seq, rank, world, group, dev, fused_allreduce=fused_allreduce,
-                gemv_impl=gemv_impl)
+    m = Qwen3TP(c, max_seq, rank, world, group, dev, fused_allreduce=fused_allreduce)
     torch.cuda.synchronize()
     t_init = time.perf_counter() - t0
     g = torch.Generator(device=dev).manual_seed(6)
@@ -409,6 +401,5 @@ def run_config5(rank=0, world=1, group=None, prompt_len=8192, gen_tokens=256, sh
             "tok_s": gen_tokens / (decode_ms * 1e-3), "step_ms": decode_ms / gen_tokens,
             "attn_ms_per_step": attn_ms, "init_s": t_init, "first_tokens": toks[:4],
             "stage_ms_per_step": stages,
-            "gemv": m.gemv_impl,
-            "allreduce": "grout NVLink P2P (o_proj and down_proj: GEMV + all-reduce + residual in one kernel)" if m.comm is not None
+            "allreduce": "grout NVLink P2P (o_proj: GEMV + all-reduce + residual in one kernel; down_proj: cuBLAS GEMV + grout all-reduce)" if m.comm is not None
                          else ("none" if world == 1 else "NCCL")}

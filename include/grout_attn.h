@@ -353,14 +353,6 @@ grout_status grout_add_rms_norm(const void* x, const void* residual, const void*
                                 grout_stream_t stream);
 grout_status grout_silu_mul(const void* gate_up, void* out, int32_t rows, int32_t n,
                             grout_stream_t stream);
-/* Decode GEMV, one token: y[n] = W x (+ residual[n], NULL = none), W [n][k]
- * f16 row-major, x [k] f16, f32 accumulation in a fixed order, one f16
- * rounding; k a multiple of 8 in [256, 32768].  Replaces the decode graph's
- * cuBLAS GEMVs (src/cublas.rs:434-470; QKV, o_proj, gate/up, down_proj at
- * src/model.rs:3248-3354): each CTA streams a contiguous block of rows with
- * bulk copies through a shared-memory ring. */
-grout_status grout_gemv(const void* w, int32_t n, int32_t k, const void* x, const void* residual,
-                        void* y, grout_stream_t stream);
 
 /* ------------------------------------------------------ paged KV caches */
 

@@ -52,25 +52,3 @@ def test_glue_validation(grout):
     with pytest.raises(grout.GroutError):  # n not a multiple of 8
         grout.add_rms_norm(x, torch.ones(12, device="cuda", dtype=torch.float16), x.clone(), 1e-6)
 
-
-@pytest.mark.parametrize("n,k", [(5120, 1024), (10240, 5120), (51200, 5120), (5120, 25600),
-                                 (1000, 3200), (8, 256), (3, 32768)])
-def test_gemv(grout, n, k):
-    """grout_gemv against torch fp32 (f32 accumulation, one f16 rounding)."""
-    g = torch.Generator(device="cuda").manual_seed(n + k)
-    w = (0.02 * torch.randn(n, k, device="cuda", generator=g)).half()
-    x = torch.randn(k, device="cuda", generator=g).half()
-    r = torch.randn(n, device="cuda", generator=g).half()
-    out = torch.empty(n, device="cuda", dtype=torch.float16)
-    grout.gemv(w, x, out, residual=r)
-    ref = w.float() @ x.float() + r.float()
-    torch.cuda.synchronize()
-    err = (out.float() - ref).abs()
-    bound = ref.abs() * 2.0 ** -10 + 1e-4 * ref.abs().max().item() + 1e-3
-    assert bool((err <= bound).all()), float((err - bound).max())
-    # deterministic: a second call gives the same bits
-    out2 = torch.empty_like(out)
-    grout.gemv(w, x, out2, residual=r)
-    torch.cuda.synchronize()
-    assert torch.equal(out, out2)
-    grout.check_device_error()
