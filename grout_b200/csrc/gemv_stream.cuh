@@ -110,9 +110,25 @@ __device__ __forceinline__ bool gemv_stream_rows(const __half* w_blk, int nrows,
       const int rs = r * cpr, re = rs + cpr;
       if (rs >= c1) break;  // the row starts in a later piece
       const int lo = max(rs, c0), hi = min(re, c1);
-      for (int c = lo + lane; c < hi; c += 32)
+      // four chunks per lane in flight (independent sums), then the rest
+      int c = lo + lane;
+      float a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      for (; c + 96 < hi; c += 128) {
+        uint4 wv[4], xv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          wv[u] = *reinterpret_cast<const uint4*>(buf + (c + 32 * u - c0) * 16);
+          xv[u] = *reinterpret_cast<const uint4*>(xs + (c + 32 * u - rs) * 8);
+        }
+        acc += gemv_dot8(wv[0], xv[0]);
+        a1 += gemv_dot8(wv[1], xv[1]);
+        a2 += gemv_dot8(wv[2], xv[2]);
+        a3 += gemv_dot8(wv[3], xv[3]);
+      }
+      for (; c < hi; c += 32)
         acc += gemv_dot8(*reinterpret_cast<const uint4*>(buf + (c - c0) * 16),
                          *reinterpret_cast<const uint4*>(xs + (c - rs) * 8));
+      acc += (a1 + a2) + a3;
       if (re > c1) break;  // the row goes on in the next piece
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
