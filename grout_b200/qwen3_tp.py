@@ -121,10 +121,10 @@ class Qwen3TP:
         self.h_last = torch.zeros(1, H, device=self.dev, dtype=torch.float16)
         nks = attn.decode_workspace_bytes(1, max_seq, self.hq, self.hkv, max_seq)
         self.ws = torch.empty(max(16, nks), dtype=torch.uint8, device=self.dev)
-        # Decode o_proj / down_proj (TP > 1), the faster of each measured on
-        # B200: o_proj as one grout kernel (GEMV + all-reduce over NVLink peer
-        # memory + residual), down_proj as a cuBLAS GEMV followed by the grout
-        # all-reduce + residual.  NCCL when disabled.
+        # Decode o_proj / down_proj (TP > 1): a cuBLAS GEMV followed by the
+        # grout all-reduce + residual over NVLink peer memory, the faster form
+        # measured on B200 at TP = 2 (the fused GEMV + all-reduce kernel's
+        # GEMV streams at about half of cuBLAS's rate).  NCCL when disabled.
         self.comm = None
         if fused_allreduce and world > 1:
             from .tp import TPComm
@@ -235,10 +235,12 @@ class Qwen3TP:
             if self.trace is not None and L is self.layers[0]:
                 self.trace["decode"] = (qkv.clone(), self.o1.clone())
             if self.comm is not None:
-                # o_proj: GEMV + all-reduce + residual in one grout kernel
+                # o_proj: cuBLAS GEMV, then the grout all-reduce + residual
+                po = self._proj(L["w_o"], self.o1)
+                mark("o_proj_gemv")
                 x1 = torch.empty_like(x)
-                self.comm.gemv_allreduce(L["w_o"], self.o1, x1, residual=x)
-                mark("o_proj_gemv_allreduce")
+                self.comm.allreduce(po, x1, residual=x)
+                mark("o_proj_allreduce")
                 h, x = self._norm(x1, L["post_norm"])
             else:
                 p = self._allreduce(self._proj(L["w_o"], self.o1))
@@ -401,5 +403,5 @@ def run_config5(rank=0, world=1, group=None, prompt_len=8192, gen_tokens=256, sh
             "tok_s": gen_tokens / (decode_ms * 1e-3), "step_ms": decode_ms / gen_tokens,
             "attn_ms_per_step": attn_ms, "init_s": t_init, "first_tokens": toks[:4],
             "stage_ms_per_step": stages,
-            "allreduce": "grout NVLink P2P (o_proj: GEMV + all-reduce + residual in one kernel; down_proj: cuBLAS GEMV + grout all-reduce)" if m.comm is not None
+            "allreduce": "grout NVLink P2P all-reduce + residual after cuBLAS GEMVs (o_proj, down_proj)" if m.comm is not None
                          else ("none" if world == 1 else "NCCL")}

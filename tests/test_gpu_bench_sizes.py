@@ -114,12 +114,17 @@ def _shard_worker(rank, world, port, q_):
         out = _c4_run(g, dev, hq, hkv, lens, cu, tot, q, k, v,
                       kv_head_range=(rank * per, (rank + 1) * per))
         G = hq // hkv
-        mine = out[:, rank * per * G:(rank + 1) * per * G].contiguous().cpu()
-        full = _c4_run(g, dev, hq, hkv, lens, cu, tot, q, k, v).cpu() if rank == 0 else None
+        # numpy (f16 bits as int16) travels by value through the queue
+        mine = out[:, rank * per * G:(rank + 1) * per * G].contiguous().cpu().view(torch.int16).numpy()
+        full = (_c4_run(g, dev, hq, hkv, lens, cu, tot, q, k, v).cpu().view(torch.int16).numpy()
+                if rank == 0 else None)
         q_.put((rank, (mine, full)))
         dist.barrier()
-    finally:
         dist.destroy_process_group()
+    finally:
+        q_.close()
+        q_.join_thread()
+    os._exit(0)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
@@ -136,5 +141,5 @@ def test_config4_kv_head_shards_on_two_gpus():
         p.join(timeout=120)
         assert p.exitcode == 0
     full = res[0][1]
-    joined = torch.cat([res[0][0], res[1][0]], 1)
-    assert torch.equal(joined.view(torch.int16), full.view(torch.int16))
+    joined = np.concatenate([res[0][0], res[1][0]], 1)
+    assert np.array_equal(joined, full)
